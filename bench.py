@@ -1,0 +1,451 @@
+#!/usr/bin/env python
+"""Flash-Born attention benchmark on B200: fwd+bwd TFLOP/s (BASELINE config C2 by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c1|c3|c4]
+
+One step = one forward + backward of Born attention over one batch of synthetic inputs resident
+in HBM (C2: B=8, H=16, N=2048, d=64, bf16, causal, per-head scale 8, eps 1e-12; Q, K, V from
+torch seed 0, dO from seed 1, drawn in fp32 then cast).  With N GPUs (one process per GPU,
+launched by torch.distributed.run) every rank runs its own C2-sized slice of a global batch of
+8N sequences (weak scaling; the (batch, head) units are independent, so there is no collective
+on the data path); value = all ranks' FLOPs / the slowest rank's device time.
+
+FLOPs are algorithmic: 14 d per valid (query, key) pair (forward QK^T and PV, backward S
+recompute, dP, dV, dK, dQ), elementwise work not counted.
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference algorithm's CPU path
+(the torch eager restatement in oracle/eager_torch.py, all host threads) on a bounded sample of
+the same workload and prints the same line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+WORKLOADS = {
+    # name: (B, H, N, D, causal, description)
+    "c1": (2, 4, 256, 64, True, "C1 B=2 H=4 N=256 d=64 causal (bf16 on GPU)"),
+    "c2": (8, 16, 2048, 64, True, "C2 B=8 H=16 N=2048 d=64 causal bf16"),
+    "c3": (1, 32, 16384, 128, True, "C3 B=1 H=32 N=16384 d=128 causal bf16, unit-norm*sqrt(d) Q/K"),
+    "c4": (4, 16, 8192, 64, True, "C4 B=4 H=16 N=8192 d=64 doc-masked bf16 (geometric doc lengths, mean 512)"),
+}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def doc_ids_geometric(B: int, N: int, mean: float, seed: int) -> np.ndarray:
+    """Per row: geometric document lengths (mean ``mean``, support >= 1) until N is covered."""
+    rng = np.random.default_rng(seed)
+    doc = np.zeros((B, N), dtype=np.int32)
+    for b in range(B):
+        t, d = 0, 0
+        while t < N:
+            L = int(rng.geometric(1.0 / mean))
+            doc[b, t:t + L] = d
+            t += L
+            d += 1
+    return doc
+
+
+def valid_pairs(workload: str, B: int, H: int, N: int, doc: np.ndarray | None) -> int:
+    if doc is None:
+        return B * H * N * (N + 1) // 2
+    total = 0
+    for b in range(B):
+        _, counts = np.unique(doc[b], return_counts=True)
+        total += int(np.sum(counts.astype(np.int64) * (counts + 1) // 2))
+    return total * H
+
+
+def make_inputs(workload: str, rank: int):
+    """CPU fp32 inputs of one rank's slice (rank 0 = the exact BASELINE recipe)."""
+    B, H, N, D, causal, _ = WORKLOADS[workload]
+    seed_qkv = {"c1": 0, "c2": 0, "c3": 2, "c4": 3}[workload] + 1000 * rank
+    torch.manual_seed(seed_qkv)
+    q = torch.randn(B, H, N, D)
+    k = torch.randn(B, H, N, D)
+    v = torch.randn(B, H, N, D)
+    if workload == "c3":
+        q = q / q.norm(dim=-1, keepdim=True) * math.sqrt(D)
+        k = k / k.norm(dim=-1, keepdim=True) * math.sqrt(D)
+    torch.manual_seed(1 + 1000 * rank)
+    do = torch.randn(B, H, N, D)
+    doc = doc_ids_geometric(B, N, 512.0, 3 + 1000 * rank) if workload == "c4" else None
+    scale = math.sqrt(D)  # the caller's head_scale init, sqrt(head_dim) (layers/attention.py:390,429)
+    return q, k, v, do, doc, scale
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of one GPU while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append([x.strip() for x in line.split(",")])
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for n, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [p for p in vis.split(",") if p.strip()]
+    if parts and all(p.strip().isdigit() for p in parts) and local_rank < len(parts):
+        return int(parts[local_rank])
+    return local_rank
+
+
+def cpu_eager_sample(workload: str, target_s: float, max_units: int | None = None):
+    """Time the reference's CPU eager algorithm on whole (batch, head) units of the workload.
+
+    Returns (flops_per_s, units, seconds, threads)."""
+    from oracle.eager_torch import eager_unit_fwd_bwd
+
+    B, H, N, D, causal, _ = WORKLOADS[workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    threads = torch.get_num_threads()
+    gen = torch.Generator().manual_seed(0)
+    doc = doc_ids_geometric(1, N, 512.0, 3)[0] if workload == "c4" else None
+    doc_t = None if doc is None else torch.from_numpy(doc)
+    pairs = valid_pairs(workload, 1, 1, N, None if doc is None else doc[None])
+    flops_unit = 14 * D * pairs
+    units, t0 = 0, time.perf_counter()
+    while True:
+        q, k, v, do = (torch.randn(N, D, generator=gen) for _ in range(4))
+        eager_unit_fwd_bwd(q, k, v, do, math.sqrt(D), causal, 1e-12, 0, doc_t)
+        units += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or (max_units is not None and units >= max_units):
+            break
+    return flops_unit * units / el, units, el, threads, flops_unit
+
+
+def run_reference_arm(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return  # under torchrun rank 0 alone runs the CPU reference
+    B, H, N, D, causal, desc = WORKLOADS[args.workload]
+    # warm-up units, then K timed steps, each a bounded sample (whole (b,h) units)
+    per_step_s = float(os.environ.get("FB_REF_STEP_SECONDS", "3.0"))
+    for _ in range(max(1, min(args.warmup, 2))):
+        cpu_eager_sample(args.workload, 0.0, max_units=1)
+    rates, secs, units_total, flops_total = [], 0.0, 0, 0.0
+    threads = 1
+    flops_unit = 0
+    for _ in range(args.steps):
+        rate, units, el, threads, flops_unit = cpu_eager_sample(args.workload, per_step_s)
+        rates.append(rate)
+        secs += el
+        units_total += units
+        flops_total += rate * el
+    value = flops_total / secs / 1e12
+    line = {
+        "impl": "reference",
+        "metric": "born_attn_fwd_bwd_tflops",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * secs / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": desc, "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{units_total} whole (batch, head) units of {args.workload} (N={N}, d={D}), "
+                                   f"{flops_unit / 1e9:.2f} GFLOP each, fp32, torch eager restatement of "
+                                   "flash_born.py:681-690 + autograd, one unit at a time"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> None:
+    import torch.distributed as dist
+
+    from quantumdlblocks_b200 import flash_born_attention
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    B, H, N, D, causal, desc = WORKLOADS[args.workload]
+    qc, kc, vc, doc_c, doc_np, scale_val = None, None, None, None, None, None
+    q_cpu, k_cpu, v_cpu, do_cpu, doc_np, scale_val = make_inputs(args.workload, rank)
+    bf = torch.bfloat16
+    q = q_cpu.to(bf).to(dev).requires_grad_(True)
+    k = k_cpu.to(bf).to(dev).requires_grad_(True)
+    v = v_cpu.to(bf).to(dev).requires_grad_(True)
+    do = do_cpu.to(bf).to(dev)
+    doc = None if doc_np is None else torch.from_numpy(doc_np).to(dev)
+    scale = torch.full((1, H, 1, 1), scale_val, device=dev, requires_grad=True)
+    pairs = valid_pairs(args.workload, B, H, N, doc_np)
+    flops_step = 14.0 * D * pairs
+
+    launches = {"fwd": 0, "bwd": 0}
+
+    def step(qq, kk, vv, dd):
+        out = flash_born_attention(qq, kk, vv, scale, is_causal=causal, eps=1e-12, doc_ids=doc)
+        launches["fwd"] = fbm.last_launch_count()
+        grads = torch.autograd.grad(out, (qq, kk, vv, scale), dd)
+        launches["bwd"] = fbm.last_launch_count()
+        return out, grads
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        step(q, k, v, do)
+    torch.cuda.synchronize()
+    rc, site = fbm.device_status()
+    if rc != 0:
+        raise RuntimeError(f"device status {rc} (site {site}) after warm-up")
+
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    time.sleep(0.3)
+    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()  # L2 flush (256 MiB > 126 MB L2), outside the per-step events
+        ev_s[i].record()
+        step(q, k, v, do)
+        ev_e[i].record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    step_ms = [ev_s[i].elapsed_time(ev_e[i]) for i in range(args.steps)]
+    t_ms = float(sum(step_ms))
+    gpu_launches = args.steps * (launches["fwd"] + launches["bwd"])
+
+    # per-kernel timing of the forward and backward launches (C-ABI through the custom ops)
+    sc_flat = scale.detach().reshape(-1).float().contiguous()
+    qd, kd, vd = q.detach(), k.detach(), v.detach()
+    reps = max(5, min(50, args.steps))
+    t_fwd, t_bwd = 0.0, 0.0
+    out_d, z_d = torch.ops.flashborn_b200.born_fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+    n_fwd_launch = fbm.last_launch_count()
+    for _ in range(reps):
+        flush.zero_()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        out_d, z_d = torch.ops.flashborn_b200.born_fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+        a1.record()
+        flush.zero_()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record()
+        torch.ops.flashborn_b200.born_bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 0, 0.0, False)
+        b1.record()
+        torch.cuda.synchronize()
+        t_fwd += a0.elapsed_time(a1)
+        t_bwd += b0.elapsed_time(b1)
+    n_bwd_launch = fbm.last_launch_count()
+    t_fwd /= reps
+    t_bwd /= reps
+    path_fwd = "tcgen05" if _path_is_tc(qd, False) else "general"
+    path_bwd = "tcgen05" if _path_is_tc(qd, True) else "general"
+
+    # end-to-end through the public API: pinned host inputs in, outputs + grads out, every step
+    e2e_steps = max(3, min(args.steps, args.e2e_steps))
+    hq, hk, hv, hdo = (x.to(bf).pin_memory() for x in (q_cpu, k_cpu, v_cpu, do_cpu))
+    h_out = [torch.empty_like(hq).pin_memory() for _ in range(4)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        xq = hq.to(dev, non_blocking=True).requires_grad_(True)
+        xk = hk.to(dev, non_blocking=True).requires_grad_(True)
+        xv = hv.to(dev, non_blocking=True).requires_grad_(True)
+        xd = hdo.to(dev, non_blocking=True)
+        out, (gq, gk, gv, _) = step(xq, xk, xv, xd)
+        for dst, src in zip(h_out, (out, gq, gk, gv)):
+            dst.copy_(src, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = 4 * hq.numel() * hq.element_size()
+    d2h = 4 * hq.numel() * hq.element_size()
+
+    # max over ranks
+    times = torch.tensor([t_ms, e2e_ms, t_fwd, t_bwd], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms, t_fwd, t_bwd = (float(x) for x in times.tolist())
+
+    peaks, peak_src = load_peaks()
+    value = world * flops_step * args.steps / (t_ms / 1e3) / 1e12
+    e2e_value = world * flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
+    flops_fwd = 4.0 * D * pairs
+    flops_bwd = 10.0 * D * pairs
+    dominant = "bwd" if t_bwd >= t_fwd else "fwd"
+    dom_flops, dom_ms = (flops_bwd, t_bwd) if dominant == "bwd" else (flops_fwd, t_fwd)
+    achieved = dom_flops / (dom_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, units, el, threads, flops_unit = cpu_eager_sample(args.workload, args.cpu_seconds)
+        cpu = {"value": rate / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{units} whole (batch, head) units of {args.workload} (N={N}, d={D}) in {el:.1f} s, "
+                         "fp32, torch eager restatement of flash_born.py:681-690 + autograd"}
+
+    if rank == 0:
+        line = {
+            "metric": "born_attn_fwd_bwd_tflops",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": t_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": desc, "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D,
+                       "parallelism": f"batch x head split, {world} rank(s), no collective",
+                       "flops_per_step_per_rank": flops_step,
+                       "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush"},
+            "per_gpu_tflops": value / world,
+            "pct_of_bf16_peak_sustained": 100.0 * value / world / float(
+                peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])),
+            "roofline": {"bound": "tensor", "kernel": f"{dominant} ({path_bwd if dominant == 'bwd' else path_fwd})",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_source": f"bf16_tflops (burst) of {peak_src}", "traffic": None,
+                         "fwd_ms": t_fwd, "bwd_ms": t_bwd, "fwd_launches": n_fwd_launch,
+                         "bwd_launches": n_bwd_launch,
+                         "fwd_tflops": flops_fwd / (t_fwd / 1e3) / 1e12,
+                         "bwd_tflops": flops_bwd / (t_bwd / 1e3) / 1e12},
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "api": "quantumdlblocks_b200.flash_born_attention + autograd"},
+            "gpu_launches": gpu_launches,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _path_is_tc(q: torch.Tensor, backward: bool) -> bool:
+    import ctypes
+
+    from quantumdlblocks_b200 import _lib
+
+    a = _lib.FbAttnArgs()
+    B, H, T, D = q.shape
+    a.batch, a.heads, a.seq_len, a.head_dim = B, H, T, D
+    a.dtype = a.out_dtype = _lib.FB_BF16
+    a.is_causal = 1
+    a.scale, a.scale_numel = 1, 1
+    for n in ("q", "k", "v", "out", "dout", "dq", "dk", "dv"):
+        setattr(a, n + "_stride", _lib._I64x4(*q.stride()))
+    return _lib.load().fb_select_path(ctypes.byref(a), int(backward)) == _lib.FB_PATH_TCGEN05
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+    else:
+        run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

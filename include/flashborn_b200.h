@@ -1,0 +1,160 @@
+/*
+ * flashborn_b200.h -- C ABI of the B200 (sm_100a) flash-Born attention library.
+ *
+ * Born attention (softmax-free; no exp, no running max):
+ *
+ *   plain     a_ij = max(0, scale_h * <q_i, k_j>) * valid(i, j)       p_ij = a_ij^2
+ *   purified  u_ij = max(0, gamma_h * (<q_i, k_j> - tau_h)) * valid,  b_ij = max(0, <q_i, k_j>) * valid
+ *             p_ij = u_ij^4 + eps_base * b_ij^2
+ *   both      Z_i = sum_j p_ij + eps          O_i = (sum_j p_ij v_j) / Z_i
+ *
+ *   valid(i, j) = (j <= i if causal) & (i - j < window if window > 0) & (doc_i == doc_j if doc ids)
+ *
+ * Every entry point replaces one host->device launch site of the reference
+ * (qdlblocks, src/qdlblocks/kernels/flash_born.py) and keeps its argument meaning:
+ *
+ *   fb_born_fwd            _flash_born_fwd_kernel[grid](...)                    flash_born.py:475-513
+ *   fb_born_bwd            _flash_born_bwd_kernel + _flash_born_bwd_dq_kernel   flash_born.py:554-612
+ *   fb_purified_born_fwd   _flash_purified_born_fwd_kernel[grid](...)          flash_born.py:1110-1147
+ *   fb_purified_born_bwd   _flash_purified_born_bwd(_dq)_kernel                 flash_born.py:1197-1262
+ *
+ * Conventions
+ *   - The caller owns every buffer (out, z, dq, dk, dv, dscale, dtau, workspace); the library
+ *     never allocates or frees device memory.
+ *   - Tensors are (B, H, T, D) with arbitrary element strides (the innermost stride must be 1 for
+ *     the tensor-core path; other layouts run on the general path). doc_ids is (B, T) int32.
+ *   - scale / tau are device fp32 vectors of 1 (shared) or H (per head) elements.
+ *   - dscale / dtau are device fp32 vectors of scale_numel / tau_numel elements; the backward
+ *     ACCUMULATES into them (zero them first, as the reference does at flash_born.py:536).
+ *   - z is (B, H, T) contiguous fp32 and holds sum_j p_ij + eps (saved for the backward).
+ *   - All work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream);
+ *     nothing synchronises the host.
+ *   - Errors are returned as FB_* status codes (never a device trap). Errors found on the device
+ *     (an mbarrier wait that ran past its bound) are latched in a device status word read by
+ *     fb_device_status().
+ */
+#ifndef FLASHBORN_B200_H_
+#define FLASHBORN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FB_API __attribute__((visibility("default")))
+#else
+#define FB_API
+#endif
+
+/* Status codes. */
+enum {
+  FB_OK = 0,
+  FB_ERR_SHAPE = 1,       /* B/H/T/D out of range, mismatched shapes */
+  FB_ERR_DTYPE = 2,       /* unsupported element type combination */
+  FB_ERR_ALIGN = 3,       /* pointer or stride alignment */
+  FB_ERR_ARG = 4,         /* null pointer, bad scale/tau length, bad window */
+  FB_ERR_LAUNCH = 5,      /* CUDA launch or attribute error (see fb_last_cuda_error) */
+  FB_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up (device status word) */
+  FB_ERR_WORKSPACE = 7,   /* workspace missing or too small */
+  FB_ERR_NO_DEVICE = 8,   /* no CUDA device / driver entry point unavailable */
+  FB_ERR_UNSUPPORTED = 9  /* no kernel for this configuration (forced path not applicable) */
+};
+
+/* Element types. */
+enum { FB_F32 = 0, FB_F16 = 1, FB_BF16 = 2 };
+
+/* Kernel path selection (fb_attn_args.path). */
+enum {
+  FB_PATH_AUTO = 0,      /* tensor-core path when applicable, else the general path */
+  FB_PATH_TCGEN05 = 1,   /* force the tcgen05/TMEM/TMA path (FB_ERR_UNSUPPORTED if not applicable) */
+  FB_PATH_GENERAL = 2    /* force the general fp32-accumulating CUDA-core path */
+};
+
+typedef struct fb_attn_args {
+  /* Problem shape. */
+  int32_t batch, heads, seq_len, head_dim;
+  /* Element type of q, k, v, dout, dq, dk, dv. */
+  int32_t dtype;
+  /* Element type of out (the forward output; the backward reads it back for delta).
+   * Plain Born: equal to dtype. Purified Born: FB_F32 (flash_born.py:1102). */
+  int32_t out_dtype;
+  int32_t is_causal;
+  int32_t window_size; /* 0 = no window; else i - j < window_size */
+  float eps;           /* added after the row sum: Z = sum p + eps */
+  float eps_base;      /* purified only: weight of the relu(raw)^2 floor */
+  int32_t path;        /* FB_PATH_* */
+  int32_t deterministic; /* 1: no floating-point atomics in the backward */
+
+  const void* q;    int64_t q_stride[4];
+  const void* k;    int64_t k_stride[4];
+  const void* v;    int64_t v_stride[4];
+  void* out;        int64_t out_stride[4];
+  float* z; /* (B, H, T) contiguous */
+
+  const float* scale; int32_t scale_numel; /* plain: scale; purified: gamma */
+  const float* tau;   int32_t tau_numel;   /* purified only */
+
+  const int32_t* doc_ids; int64_t doc_stride[2]; /* NULL = no document mask */
+
+  /* Backward only. */
+  const void* dout; int64_t dout_stride[4];
+  void* dq;         int64_t dq_stride[4];
+  void* dk;         int64_t dk_stride[4];
+  void* dv;         int64_t dv_stride[4];
+  float* dscale; /* accumulated, scale_numel elements */
+  float* dtau;   /* accumulated, tau_numel elements (purified) */
+
+  void* workspace; size_t workspace_bytes;
+} fb_attn_args;
+
+/* Plain flash-Born forward: writes out and z. Replaces flash_born.py:475-513. */
+FB_API int fb_born_fwd(const fb_attn_args* args, void* stream);
+
+/* Plain flash-Born backward: writes dq, dk, dv; accumulates dscale.
+ * Replaces flash_born.py:554-612 (dK/dV/dscale kernel + dQ kernel). */
+FB_API int fb_born_bwd(const fb_attn_args* args, void* stream);
+
+/* Purified (degree-4 thresholded) forward. Replaces flash_born.py:1110-1147. */
+FB_API int fb_purified_born_fwd(const fb_attn_args* args, void* stream);
+
+/* Purified backward: dq, dk, dv; accumulates dscale (d gamma) and dtau.
+ * Replaces flash_born.py:1197-1262. */
+FB_API int fb_purified_born_bwd(const fb_attn_args* args, void* stream);
+
+/* Bytes of device workspace the backward needs for these arguments (0 allowed for none).
+ * A non-NULL tau marks purified arguments here and in fb_select_path.
+ * The reference allocates the equivalent scratch implicitly (delta is recomputed per tile). */
+FB_API size_t fb_bwd_workspace_size(const fb_attn_args* args);
+
+/* Which path fb_*_fwd / fb_*_bwd would take for these arguments: FB_PATH_TCGEN05 or
+ * FB_PATH_GENERAL, or a negative FB_ERR_* if the arguments are invalid. `backward` selects
+ * the backward kernels. Replaces get_flash_born_launch_meta (flash_born.py:31-65) as the
+ * host-visible tile policy. */
+FB_API int fb_select_path(const fb_attn_args* args, int backward);
+
+/* Number of kernel launches the last successful fb_* call on this host thread enqueued. */
+FB_API int fb_last_launch_count(void);
+
+/* Reads (and clears) the device status word of the current device: FB_OK or FB_ERR_TIMEOUT.
+ * Synchronises `stream`. `detail` (may be NULL) receives the site code of the first failure. */
+FB_API int fb_device_status(void* stream, int32_t* detail);
+
+/* Human-readable message for a status code. */
+FB_API const char* fb_strerror(int status);
+
+/* The last CUDA runtime error string seen by the library on this host thread. */
+FB_API const char* fb_last_cuda_error(void);
+
+/* FB_ABI_VERSION of the built library. */
+FB_API int fb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHBORN_B200_H_ */

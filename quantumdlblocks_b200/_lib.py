@@ -1,0 +1,119 @@
+"""ctypes binding of libflashborn_b200.so (the C ABI declared in include/flashborn_b200.h).
+
+The library is built in-tree by ``python -m quantumdlblocks_b200.build`` (or
+``__graft_entry__.build()``).  Loading it needs no GPU; running its entry points does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libflashborn_b200.so")
+
+FB_OK = 0
+FB_ERR_SHAPE = 1
+FB_ERR_DTYPE = 2
+FB_ERR_ALIGN = 3
+FB_ERR_ARG = 4
+FB_ERR_LAUNCH = 5
+FB_ERR_TIMEOUT = 6
+FB_ERR_WORKSPACE = 7
+FB_ERR_NO_DEVICE = 8
+FB_ERR_UNSUPPORTED = 9
+
+FB_F32, FB_F16, FB_BF16 = 0, 1, 2
+FB_PATH_AUTO, FB_PATH_TCGEN05, FB_PATH_GENERAL = 0, 1, 2
+
+_I64x4 = ctypes.c_int64 * 4
+_I64x2 = ctypes.c_int64 * 2
+
+
+class FbAttnArgs(ctypes.Structure):
+    """Mirror of ``fb_attn_args`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("is_causal", ctypes.c_int32), ("window_size", ctypes.c_int32),
+        ("eps", ctypes.c_float), ("eps_base", ctypes.c_float),
+        ("path", ctypes.c_int32), ("deterministic", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_stride", _I64x4),
+        ("k", ctypes.c_void_p), ("k_stride", _I64x4),
+        ("v", ctypes.c_void_p), ("v_stride", _I64x4),
+        ("out", ctypes.c_void_p), ("out_stride", _I64x4),
+        ("z", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p), ("scale_numel", ctypes.c_int32),
+        ("tau", ctypes.c_void_p), ("tau_numel", ctypes.c_int32),
+        ("doc_ids", ctypes.c_void_p), ("doc_stride", _I64x2),
+        ("dout", ctypes.c_void_p), ("dout_stride", _I64x4),
+        ("dq", ctypes.c_void_p), ("dq_stride", _I64x4),
+        ("dk", ctypes.c_void_p), ("dk_stride", _I64x4),
+        ("dv", ctypes.c_void_p), ("dv_stride", _I64x4),
+        ("dscale", ctypes.c_void_p), ("dtau", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+# Every symbol the header declares, with its ctypes signature.
+_PARGS = ctypes.POINTER(FbAttnArgs)
+SIGNATURES = {
+    "fb_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_purified_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_purified_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_bwd_workspace_size": (ctypes.c_size_t, [_PARGS]),
+    "fb_select_path": (ctypes.c_int, [_PARGS, ctypes.c_int]),
+    "fb_last_launch_count": (ctypes.c_int, []),
+    "fb_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]),
+    "fb_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "fb_last_cuda_error": (ctypes.c_char_p, []),
+    "fb_abi_version": (ctypes.c_int, []),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class FlashBornLibraryError(RuntimeError):
+    """The native library is missing or returned an error status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the native library; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise FlashBornLibraryError(
+                    f"{LIB_PATH} is missing: build it with `python -m quantumdlblocks_b200.build` "
+                    "(the flash-Born op has no fallback path)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = argtypes
+            _lib = lib
+    return _lib
+
+
+def available() -> bool:
+    try:
+        load()
+        return True
+    except (OSError, FlashBornLibraryError):
+        return False
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FB_OK:
+        lib = load()
+        msg = lib.fb_strerror(rc).decode()
+        if rc == FB_ERR_LAUNCH:
+            msg += f" [{lib.fb_last_cuda_error().decode()}]"
+        exc = ValueError if rc in (FB_ERR_SHAPE, FB_ERR_DTYPE, FB_ERR_ARG) else FlashBornLibraryError
+        raise exc(f"{what}: {msg} (status {rc})")

@@ -1,0 +1,136 @@
+// fb_common.cuh -- shared definitions of the flash-Born CUDA library (sm_100a).
+//
+// Element conversion, the two Born pointwise maps (plain and purified), the validity mask and
+// the normalised problem description that the C-ABI layer (fb_abi.cu) hands to the kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/flashborn_b200.h"
+
+namespace fb {
+
+// ------------------------------------------------------------------------------------------
+// Normalised problem (host side; passed by value to kernels as needed)
+// ------------------------------------------------------------------------------------------
+struct Tensor4 {
+  const void* ptr;
+  int64_t s[4];  // element strides for (B, H, T, D)
+};
+
+struct Problem {
+  int B, H, T, D;
+  int dtype, out_dtype;
+  bool causal;
+  int window;
+  float eps, eps_base;
+  bool purified;
+  Tensor4 q, k, v, o, dout, dq, dk, dv;
+  float* z;
+  const float* scale;
+  int scale_per_head;
+  const float* tau;
+  int tau_per_head;
+  const int32_t* doc;
+  int64_t doc_s[2];
+  float* dscale;
+  float* dtau;
+  void* ws;
+  size_t ws_bytes;
+  int* status;  // device status word [2]: {code, site}
+};
+
+// Device status codes written into Problem::status.
+enum : int { kStatusOk = 0, kStatusTimeout = FB_ERR_TIMEOUT };
+
+// ------------------------------------------------------------------------------------------
+// Element conversion
+// ------------------------------------------------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// ------------------------------------------------------------------------------------------
+// Validity of a (query i, key j) pair: flash_born.py:169-178 / :635-652.
+//   causal: j <= i;  window > 0: i - j < window (a non-causal window leaves the future visible);
+//   document ids: equal.  Keys at or beyond T are never valid.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ bool pair_valid(int i, int j, int T, bool causal, int window, int doc_i, int doc_j) {
+  bool ok = j < T;
+  if (causal) ok = ok && (j <= i);
+  if (window > 0) ok = ok && (i - j < window);
+  return ok && (doc_i == doc_j);
+}
+
+// ------------------------------------------------------------------------------------------
+// Pointwise maps.  raw = <q_i, k_j> (unscaled).  prob() gives p_ij; grad() turns
+// dP_ij = dL/dp_ij into dL/draw_ij and accumulates the parameter gradients.
+// ------------------------------------------------------------------------------------------
+struct PlainMap {
+  float scale;
+  // a = relu(scale * raw), p = a^2                                      flash_born.py:166-181
+  __device__ __forceinline__ float prob(float raw, bool valid) const {
+    float a = valid ? fmaxf(raw * scale, 0.f) : 0.f;
+    return a * a;
+  }
+  // dS = 2 a dP (masked), dscale += dS * raw, dL/draw = dS * scale      flash_born.py:306-312
+  __device__ __forceinline__ float grad(float raw, bool valid, float dp, float& g1, float& g2) const {
+    (void)g2;
+    if (!valid) return 0.f;
+    float a = fmaxf(raw * scale, 0.f);
+    float ds = 2.f * a * dp;
+    g1 += ds * raw;
+    return ds * scale;
+  }
+};
+
+struct PurifiedMap {
+  float gamma, tau, eps_base;
+  // u = relu(gamma (raw - tau)), b = relu(raw), p = u^4 + eps_base b^2  flash_born.py:782-797
+  __device__ __forceinline__ float prob(float raw, bool valid) const {
+    if (!valid) return 0.f;
+    float u = fmaxf(gamma * (raw - tau), 0.f);
+    float b = fmaxf(raw, 0.f);
+    float u2 = u * u;
+    return u2 * u2 + eps_base * (b * b);
+  }
+  // du = 4 u^3 dP; dL/draw = du gamma + 2 eps_base b dP;
+  // dgamma += du (raw - tau); dtau += -du gamma                         flash_born.py:930-937
+  __device__ __forceinline__ float grad(float raw, bool valid, float dp, float& g1, float& g2) const {
+    if (!valid) return 0.f;
+    float u = fmaxf(gamma * (raw - tau), 0.f);
+    float b = fmaxf(raw, 0.f);
+    float du = 4.f * (u * u * u) * dp;
+    g1 += du * (raw - tau);
+    g2 += -du * gamma;
+    return du * gamma + 2.f * eps_base * b * dp;
+  }
+};
+
+__device__ __forceinline__ void set_status(int* status, int code, int site) {
+  if (status != nullptr && atomicCAS(status, 0, code) == 0) status[1] = site;
+}
+
+}  // namespace fb
+
+// Internal host-side launchers (defined in fb_general.cu / fb_tc_*.cu).
+namespace fb {
+int general_fwd(const Problem& p, cudaStream_t s, int* launches);
+int general_bwd(const Problem& p, cudaStream_t s, int* launches);
+size_t general_bwd_workspace(const Problem& p);
+bool tc_fwd_supported(const Problem& p);
+int tc_fwd(const Problem& p, cudaStream_t s, int* launches);
+bool tc_bwd_supported(const Problem& p);
+int tc_bwd(const Problem& p, cudaStream_t s, int* launches);
+size_t tc_bwd_workspace(const Problem& p);
+void record_cuda_error(cudaError_t e);
+}  // namespace fb

@@ -1,0 +1,53 @@
+"""Host-side logic of the drop-in module (no GPU)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import quantumdlblocks_b200 as fbk
+from quantumdlblocks_b200.kernels import flash_born as fbm
+
+
+def test_public_names_match_reference_surface():
+    # qdlblocks.kernels re-exports these names for flash-Born (kernels/__init__.py:3-10)
+    for name in ("HAS_TRITON", "IS_HIP", "flash_born_attention", "flash_purified_born_attention",
+                 "get_flash_born_launch_meta", "get_rdna4_autotune_configs"):
+        assert hasattr(fbk, name)
+        assert hasattr(fbk.kernels, name)
+    assert fbk.IS_HIP is False
+    assert fbk.HAS_TRITON is True  # the library is built in-tree
+
+
+def test_launch_metadata_pins_of_the_reference_tests():
+    # tests/test_flash_born.py:70-83 of the reference
+    hip = fbk.get_flash_born_launch_meta(64, is_hip=True)
+    assert hip["num_warps"] == 4 and hip["waves_per_eu"] == 2
+    cuda = fbk.get_flash_born_launch_meta(64, is_hip=False)
+    assert cuda["num_warps"] == 4 and "waves_per_eu" not in cuda
+    cfgs = fbk.get_rdna4_autotune_configs()
+    assert len(cfgs) == 4
+    assert all(c["matrix_instr_nonkdim"] == 16 and c["waves_per_eu"] in (2, 4) for c in cfgs)
+    # tests/test_plan049_...py:308-319 of the reference
+    assert fbk.get_flash_born_launch_meta(512, head_dim=64)["BLOCK_M"] == 64
+    assert fbk.get_flash_born_launch_meta(512, head_dim=64)["BLOCK_N"] == 64
+    for hd in (48, 80, 96, 112):
+        assert fbk.get_flash_born_launch_meta(512, head_dim=hd)["BLOCK_M"] in (32, 64)
+
+
+def test_cpu_tensors_raise_no_fallback():
+    x = torch.randn(1, 2, 8, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fbk.flash_born_attention(x, x, x, 1.0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fbk.flash_purified_born_attention(x, x, x)
+
+
+def test_kernel_path_override():
+    assert fbm.get_kernel_path() == "auto"
+    fbm.set_kernel_path("general")
+    try:
+        assert fbm.get_kernel_path() == "general"
+    finally:
+        fbm.set_kernel_path("auto")
+    with pytest.raises(ValueError):
+        fbm.set_kernel_path("triton")

@@ -1,0 +1,118 @@
+"""Pin the numpy oracle against golden vectors produced by the reference itself.
+
+The reference (qdlblocks ``flash_born_attention`` / ``flash_purified_born_attention``, eager CPU
+path + autograd, run in float64 by tests/golden/make_golden.py) produced every ``ref_*`` array.
+The oracle restates the analytic backward of the reference's Triton kernels; agreement here is
+what licenses using it as the checker for the CUDA kernels.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from golden_cases import c1_inputs, case_names, load_case, manifest
+from oracle import flash_born_oracle as orc
+
+# golden outputs are float64 results rounded to float32 -> compare at float32 resolution
+RTOL = 2e-6
+
+
+def _close(x, ref, name, scale_floor=1e-30):
+    ref = np.asarray(ref, dtype=np.float64)
+    x = np.asarray(x, dtype=np.float64)
+    denom = max(np.abs(ref).max(), scale_floor)
+    err = np.abs(x - ref).max() / denom
+    assert err <= RTOL, f"{name}: max-rel {err:.3e}"
+
+
+def _run_oracle(c):
+    q, k, v, do = (c[n].astype(np.float64) for n in ("q", "k", "v", "do"))
+    if c["kind"] == "plain":
+        out, z = orc.born_forward(q, k, v, c["param_scale"].astype(np.float64), c["is_causal"], c["eps"],
+                                  c["window_size"], c["doc_ids"])
+        g = orc.born_backward(q, k, v, out, z, do, c["param_scale"].astype(np.float64), c["is_causal"],
+                              c["window_size"], c["doc_ids"])
+    else:
+        out, z = orc.purified_forward(q, k, v, c["param_scale"].astype(np.float64),
+                                      c["param_tau"].astype(np.float64), c["eps_base"], c["is_causal"], c["eps"],
+                                      c["window_size"], c["doc_ids"])
+        g = orc.purified_backward(q, k, v, out, z, do, c["param_scale"].astype(np.float64),
+                                  c["param_tau"].astype(np.float64), c["eps_base"], c["is_causal"],
+                                  c["window_size"], c["doc_ids"])
+    return out, z, g
+
+
+def _fold(per_head, shape):
+    """Per-head oracle gradient -> the shape of the reference's parameter."""
+    n = int(np.prod(shape)) if len(shape) else 1
+    return per_head.sum().reshape(shape) if n == 1 else per_head.reshape(shape)
+
+
+@pytest.mark.parametrize("name", case_names())
+def test_oracle_matches_reference_golden(name):
+    c = load_case(name)
+    out, z, g = _run_oracle(c)
+    _close(out, c["ref_out"], "out")
+    _close(g.dq, c["ref_dq"], "dq")
+    _close(g.dk, c["ref_dk"], "dk")
+    _close(g.dv, c["ref_dv"], "dv")
+    # parameter grads: absolute check at the scale of the other gradients (dscale is ~0 for the
+    # plain op with eps=1e-12: it equals sum delta * 2 eps / (scale Z))
+    gscale = max(np.abs(c["ref_dq"]).max(), 1.0)
+    dsc = _fold(g.dscale, c["param_scale"].shape)
+    assert np.abs(dsc - c["ref_dscale"]).max() <= 1e-5 * gscale, (dsc, c["ref_dscale"])
+    if c["kind"] == "purified":
+        dta = _fold(g.dtau, c["param_tau"].shape)
+        assert np.abs(dta - c["ref_dtau"]).max() <= 1e-5 * max(np.abs(c["ref_dtau"]).max(), 1.0)
+
+
+def test_oracle_masked_entries_are_exact_zero_and_rows_normalise():
+    """The reference's mask test: masked weights are exactly 0, valid rows sum to 1."""
+    c = load_case("plain_window4_doc_t8")
+    q, k = c["q"].astype(np.float64), c["k"].astype(np.float64)
+    T = q.shape[2]
+    eye = np.eye(T)[None, None].repeat(q.shape[0], 0).repeat(q.shape[1], 1)
+    # out with V = identity rows recovers the weight matrix
+    w, _ = orc.born_forward(q, k, eye, 10.0, True, 1e-12, 4, c["doc_ids"])
+    doc = c["doc_ids"]
+    for b in range(q.shape[0]):
+        for i in range(T):
+            for j in range(T):
+                if j > i or i - j >= 4 or doc[b, i] != doc[b, j]:
+                    assert np.all(w[b, :, i, j] == 0.0)
+    np.testing.assert_allclose(w.sum(-1), 1.0, atol=1e-5)
+
+
+def test_oracle_c1_checksums():
+    """Oracle on the C1 benchmark inputs against the reference's own C1 checksums (float64)."""
+    m = manifest()["C1"]
+    q, k, v, do = (x.double().numpy() for x in c1_inputs())
+    out, z = orc.born_forward(q, k, v, np.full(4, 8.0), True, 1e-12)
+    g = orc.born_backward(q, k, v, out, z, do, np.full(4, 8.0), True)
+    ref = m["checksums"]["f64"]
+    idx = np.array(m["checksums"]["sample_idx"])
+    for name, arr in (("out", out), ("dq", g.dq), ("dk", g.dk), ("dv", g.dv)):
+        a = arr.reshape(-1)
+        r = ref[name]
+        assert abs(a.sum() - r["sum"]) <= 1e-8 * max(1.0, r["maxabs"] * a.size ** 0.5)
+        assert abs((a * a).sum() - r["sumsq"]) <= 1e-9 * r["sumsq"]
+        np.testing.assert_allclose(a[idx], np.array(r["sample"]), rtol=1e-9, atol=1e-9 * r["maxabs"])
+    np.testing.assert_allclose(g.dscale, ref["dscale"], atol=1e-9)
+
+
+def test_document_ids_from_eot_tokens():
+    """``compute_document_ids`` semantics from the reference's mask test."""
+    idx = np.array([[10, 20, 50256, 30, 40, 50256, 50, 60], [11, 50256, 22, 33, 44, 55, 66, 77]])
+    expect = np.array([[0, 0, 0, 1, 1, 1, 2, 2], [0, 0, 1, 1, 1, 1, 1, 1]], dtype=np.int32)
+    np.testing.assert_array_equal(orc.compute_document_ids(idx), expect)
+
+
+def test_count_valid_pairs_matches_mask():
+    rng = np.random.default_rng(0)
+    doc = np.sort(rng.integers(0, 5, size=50)).astype(np.int32)
+    for causal in (True, False):
+        for w in (0, 1, 7):
+            for d in (None, doc):
+                m = orc.valid_mask(np.arange(50), np.arange(50), causal, w, d, d)
+                assert orc.count_valid_pairs(50, causal, w, d) == int(m.sum())
+    assert orc.count_valid_pairs(2048, True, 0, None) == 2048 * 2049 // 2
