@@ -1,0 +1,106 @@
+"""GPU: the tcgen05 tensor-core kernels against the float64 oracle and the general CUDA path,
+forced explicitly (FB_PATH_TCGEN05), across masks, ragged lengths, both head dims and both maps."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import flash_born_oracle as orc
+from parity_util import lowp_gate, round_to
+from quantumdlblocks_b200.kernels import flash_born as fbm
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("CUDA device required", allow_module_level=True)
+
+
+def _fwd(q, k, v, scale, tau, doc, causal, window, purified, path):
+    prev = fbm.get_kernel_path()
+    fbm.set_kernel_path(path)
+    try:
+        out, z = torch.ops.flashborn_b200.born_fwd(q, k, v, scale, tau, doc, causal, 1e-12 if not purified else 1e-8,
+                                                   window, 0.05, purified)
+        launches = fbm.last_launch_count()
+        torch.cuda.synchronize()
+    finally:
+        fbm.set_kernel_path(prev)
+    return out, z, launches
+
+
+CASES = [
+    # B, H, T, D, causal, window, doc_mean
+    (1, 1, 128, 64, True, 0, None),
+    (1, 2, 1, 64, True, 0, None),
+    (2, 2, 77, 64, True, 0, None),
+    (1, 2, 300, 128, True, 0, None),
+    (2, 3, 1000, 64, True, 0, None),
+    (1, 2, 513, 64, False, 0, None),
+    (1, 2, 700, 64, True, 100, None),
+    (1, 2, 700, 128, False, 260, None),
+    (2, 2, 900, 64, True, 0, 120.0),
+    (1, 2, 640, 128, True, 0, 60.0),
+]
+
+
+@pytest.mark.parametrize("purified", [False, True])
+@pytest.mark.parametrize("case", CASES, ids=[str(c) for c in CASES])
+def test_tc_forward_matches_oracle_and_general(case, purified):
+    B, H, T, D, causal, window, doc_mean = case
+    rng = np.random.default_rng(B * 7 + T + D)
+    q, k, v = (rng.standard_normal((B, H, T, D)) for _ in range(3))
+    if purified:
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    q, k, v = (round_to(x, torch.bfloat16) for x in (q, k, v))
+    doc = None
+    if doc_mean is not None:
+        doc = np.zeros((B, T), np.int32)
+        for b in range(B):
+            t, d = 0, 0
+            while t < T:
+                L = int(rng.geometric(1 / doc_mean))
+                doc[b, t:t + L] = d
+                t, d = t + L, d + 1
+    scale = np.linspace(6.0, 9.0, H).astype(np.float32) if purified else np.linspace(0.3, 0.5, H).astype(np.float32)
+    tau = np.linspace(0.02, 0.08, H).astype(np.float32) if purified else None
+    dev = "cuda"
+    qt, kt, vt = (torch.tensor(x, dtype=torch.float32, device=dev).to(torch.bfloat16) for x in (q, k, v))
+    st = torch.tensor(scale, device=dev)
+    tt = None if tau is None else torch.tensor(tau, device=dev)
+    dt = None if doc is None else torch.tensor(doc, device=dev)
+    o_tc, z_tc, n_tc = _fwd(qt, kt, vt, st, tt, dt, causal, window, purified, "tcgen05")
+    o_ge, z_ge, _ = _fwd(qt, kt, vt, st, tt, dt, causal, window, purified, "general")
+    assert n_tc == 1
+    assert fbm.device_status() == (0, 0)
+    if purified:
+        ref, zref = orc.purified_forward(q, k, v, scale, tau, 0.05, causal, 1e-8, window, doc)
+    else:
+        ref, zref = orc.born_forward(q, k, v, scale, causal, 1e-12, window, doc)
+    o_tc_np = o_tc.double().cpu().numpy()
+    lowp_gate(o_tc_np, ref, "out(tcgen05)")
+    lowp_gate(o_ge.double().cpu().numpy(), ref, "out(general)")
+    # Z: fp32 sums of the same fp32 p (only accumulation order differs)
+    np.testing.assert_allclose(z_tc.double().cpu().numpy(), zref, rtol=2e-3, atol=1e-30)
+    np.testing.assert_allclose(z_tc.cpu().numpy(), z_ge.cpu().numpy(), rtol=2e-3)
+
+
+def test_tc_forward_is_selected_for_bf16_d64_d128():
+    x = torch.randn(1, 1, 64, 64, device="cuda", dtype=torch.bfloat16)
+    fbm.flash_born_attention(x, x, x, 1.0)
+    assert fbm.last_launch_count() == 1
+    import ctypes
+
+    from quantumdlblocks_b200 import _lib
+
+    a = _lib.FbAttnArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim = 1, 1, 64, 64
+    a.dtype = a.out_dtype = _lib.FB_BF16
+    a.scale, a.scale_numel = x.data_ptr(), 1
+    for n in ("q", "k", "v", "out"):
+        setattr(a, n, x.data_ptr())
+        setattr(a, n + "_stride", _lib._I64x4(*x.stride()))
+    assert _lib.load().fb_select_path(ctypes.byref(a), 0) == _lib.FB_PATH_TCGEN05
+    a.dtype = a.out_dtype = _lib.FB_F16
+    assert _lib.load().fb_select_path(ctypes.byref(a), 0) == _lib.FB_PATH_GENERAL
