@@ -268,6 +268,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         return out, grads
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    if args.mode != "step":
+        run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev)
+        return
     for _ in range(args.warmup):
         step(q, k, v, do)
     torch.cuda.synchronize()
@@ -407,6 +410,43 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev) -> None:
+    """--mode fwd|bwd: launch only the forward or only the backward kernels through the custom
+    ops (one C-ABI call per step), W warm-up + K timed launches, for profilers and kernel timing."""
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+
+    sc_flat = scale.detach().reshape(-1).float().contiguous()
+    qd, kd, vd = q.detach(), k.detach(), v.detach()
+    fwd = torch.ops.flashborn_b200.born_fwd
+    bwd = torch.ops.flashborn_b200.born_bwd
+    out_d, z_d = fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+
+    def one():
+        if args.mode == "fwd":
+            fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+        else:
+            bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 0, 0.0, False)
+
+    for _ in range(args.warmup):
+        one()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        one()
+        e1.record()
+        torch.cuda.synchronize()
+        total += e0.elapsed_time(e1)
+    ms = total / args.steps
+    flops = (4.0 if args.mode == "fwd" else 10.0) * D * pairs
+    rc, site = fbm.device_status()
+    if rank == 0:
+        print(json.dumps({"mode": args.mode, "workload": args.workload, "ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+                          "launches": fbm.last_launch_count(), "device_status": rc}), flush=True)
+
+
 def _path_is_tc(q: torch.Tensor, backward: bool) -> bool:
     import ctypes
 
@@ -433,6 +473,8 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["step", "fwd", "bwd"], default="step",
+                    help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

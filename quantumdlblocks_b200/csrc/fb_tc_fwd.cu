@@ -258,40 +258,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       // whole tile valid?  (below the causal diagonal, inside the window, inside T, no doc ids)
       const bool full = !kHasDoc && (!p.causal || n0 + kBN - 1 <= m0) &&
                         (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (n0 + kBN <= p.T);
-      uint32_t packed[kBN / 2];
-#pragma unroll
+      if (j >= 2) {  // P[sb] is free once O += P_{j-2} V_{j-2} has completed
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, wc, 8));
+        if (!ok) break;
+      }
+      // Compact loop (not unrolled over chunks): the pointwise warps must stay inside the
+      // instruction cache; a fully unrolled 128-column body with both mask variants does not.
+#pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(lane_addr + Cfg::kTmemS + sb * kBN + c * 32, r);
         tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pr[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float s = __uint_as_float(r[e + u]);
-            bool valid = true;
-            if (!full) {
-              const int kj = n0 + c * 32 + e + u;
-              int doc_j = 0;
-              if constexpr (kHasDoc) doc_j = docs_k[sb * kBN + c * 32 + e + u];
-              valid = pair_valid(qi, kj, p.T, p.causal, p.window, doc_i, doc_j);
-            }
-            pr[u] = map.prob(s, valid);
-            zsum += pr[u];
-          }
-          packed[c * 16 + e / 2] = pack2<true>(pr[0], pr[1]);
-        }
-      }
-      if (j >= 2) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, wc, 8));
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
         uint32_t w[16];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) w[e] = packed[c * 16 + e];
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = map.prob(__uint_as_float(r[e]), true);
+            const float p1 = map.prob(__uint_as_float(r[e + 1]), true);
+            zsum += p0 + p1;
+            w[e / 2] = pack2<true>(p0, p1);
+          }
+        } else {
+          const int kbase = n0 + c * 32;
+          const int* dk = docs_k + sb * kBN + c * 32;
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float pr[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              int doc_j = 0;
+              if constexpr (kHasDoc) doc_j = dk[e + u];
+              const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
+              pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
+            }
+            zsum += pr[0] + pr[1];
+            w[e / 2] = pack2<true>(pr[0], pr[1]);
+          }
+        }
         tmem_st16(lane_addr + Cfg::kTmemP + sb * (kBN / 2) + c * 16, w);
       }
       tmem_wait_st();

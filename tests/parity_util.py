@@ -103,8 +103,8 @@ def round_to(x, dtype) -> np.ndarray:
     return torch.as_tensor(np.asarray(x), dtype=torch.float32).to(dtype).to(torch.float64).numpy()
 
 
-def check_all(got, ref, lowp: bool, names=("out", "dq", "dk", "dv")) -> None:
-    floor = 1e-3 * max(float(np.abs(ref["out"]).max()), float(np.abs(ref["dv"]).max()))
+def check_all(got, ref, lowp: bool, names=("out", "dq", "dk", "dv"), floor_rel: float = 1e-3) -> None:
+    floor = floor_rel * max(float(np.abs(ref["out"]).max()), float(np.abs(ref["dv"]).max()))
     for n in names:
         if lowp:
             lowp_gate(got[n], ref[n], n, floor=floor)

@@ -98,6 +98,7 @@ def test_tc_forward_is_selected_for_bf16_d64_d128():
     a.batch, a.heads, a.seq_len, a.head_dim = 1, 1, 64, 64
     a.dtype = a.out_dtype = _lib.FB_BF16
     a.scale, a.scale_numel = x.data_ptr(), 1
+    a.z = x.data_ptr()
     for n in ("q", "k", "v", "out"):
         setattr(a, n, x.data_ptr())
         setattr(a, n + "_stride", _lib._I64x4(*x.stride()))
