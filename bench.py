@@ -313,7 +313,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         flush.zero_()
         b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         b0.record()
-        torch.ops.flashborn_b200.born_bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 0, 0.0, False)
+        torch.ops.flashborn_b200.born_bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
         b1.record()
         torch.cuda.synchronize()
         t_fwd += a0.elapsed_time(a1)
@@ -425,7 +425,7 @@ def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs,
         if args.mode == "fwd":
             fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
         else:
-            bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 0, 0.0, False)
+            bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
 
     for _ in range(args.warmup):
         one()

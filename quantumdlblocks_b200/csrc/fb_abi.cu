@@ -56,8 +56,9 @@ int check_tensor(const void* p, const int64_t* st) {
   return FB_OK;
 }
 
-// Validates and normalises.  backward selects the extra backward checks.
-int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p) {
+// Validates and normalises.  backward selects the extra backward checks; query_only (workspace
+// and path queries) fills the backward fields without requiring their pointers.
+int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, bool query_only = false) {
   if (a == nullptr) return FB_ERR_ARG;
   *p = Problem{};
   p->B = a->batch; p->H = a->heads; p->T = a->seq_len; p->D = a->head_dim;
@@ -89,7 +90,7 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p) {
   p->q = t4(a->q, a->q_stride); p->k = t4(a->k, a->k_stride); p->v = t4(a->v, a->v_stride);
   p->o = t4(a->out, a->out_stride);
   p->z = a->z;
-  if (!empty) {
+  if (!empty && !query_only) {
     int rc;
     if ((rc = check_tensor(a->q, a->q_stride)) || (rc = check_tensor(a->k, a->k_stride)) ||
         (rc = check_tensor(a->v, a->v_stride)) || (rc = check_tensor(a->out, a->out_stride)))
@@ -101,7 +102,7 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p) {
     p->dq = t4(a->dq, a->dq_stride); p->dk = t4(a->dk, a->dk_stride); p->dv = t4(a->dv, a->dv_stride);
     p->dscale = a->dscale; p->dtau = a->dtau;
     p->ws = a->workspace; p->ws_bytes = a->workspace_bytes;
-    if (!empty) {
+    if (!empty && !query_only) {
       int rc;
       if ((rc = check_tensor(a->dout, a->dout_stride)) || (rc = check_tensor(a->dq, a->dq_stride)) ||
           (rc = check_tensor(a->dk, a->dk_stride)) || (rc = check_tensor(a->dv, a->dv_stride)))
@@ -170,7 +171,7 @@ int fb_purified_born_bwd(const fb_attn_args* args, void* stream) { return fb::ru
 size_t fb_bwd_workspace_size(const fb_attn_args* args) {
   fb::Problem p;
   const bool purified = args != nullptr && args->tau != nullptr;
-  if (fb::normalise(args, purified, false, &p) != FB_OK) return 0;
+  if (fb::normalise(args, purified, true, &p, true) != FB_OK) return 0;
   const int path = fb::choose_path(args, p, true);
   if (path < 0) return 0;
   return fb::workspace_for(p, path);
@@ -179,7 +180,7 @@ size_t fb_bwd_workspace_size(const fb_attn_args* args) {
 int fb_select_path(const fb_attn_args* args, int backward) {
   fb::Problem p;
   const bool purified = args != nullptr && args->tau != nullptr;
-  int rc = fb::normalise(args, purified, false, &p);
+  int rc = fb::normalise(args, purified, backward != 0, &p, true);
   if (rc != FB_OK) return -rc;
   return fb::choose_path(args, p, backward != 0);
 }

@@ -4,6 +4,7 @@
 // the normalised problem description that the C-ABI layer (fb_abi.cu) hands to the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -93,6 +94,19 @@ struct PlainMap {
   }
 };
 
+// Plain map without the in-loop dscale sum: the tensor-core backward takes dscale from the exact
+// closed form  sum_ij dS_ij raw_ij = sum_i 2 eps delta_i / (scale Z_i)  (a raw = p / scale and
+// sum_j p_ij dO_i.v_j / Z_i = delta_i), which avoids the O(N^2) cancelling sum.
+struct PlainMapNoParam : PlainMap {
+  __device__ __forceinline__ float grad(float raw, bool valid, float dp, float& g1, float& g2) const {
+    (void)g1;
+    (void)g2;
+    if (!valid) return 0.f;
+    float a = fmaxf(raw * scale, 0.f);
+    return 2.f * a * dp * scale;
+  }
+};
+
 struct PurifiedMap {
   float gamma, tau, eps_base;
   // u = relu(gamma (raw - tau)), b = relu(raw), p = u^4 + eps_base b^2  flash_born.py:782-797
@@ -116,6 +130,23 @@ struct PurifiedMap {
   }
 };
 
+// Purified map for the tensor-core backward: d gamma via the identity
+//   sum_j u^4 dP = delta eps / Z - eps_base sum_j b^2 dP      (p = u^4 + eps_base b^2)
+// so  d gamma = sum du (raw - tau) = (4 / gamma) (sum_i eps delta_i / Z_i - eps_base sum b^2 dP):
+// g1 accumulates eps_base b^2 dP (small terms) instead of the cancelling du (raw - tau); the
+// closed-form part comes from the backward pre-pass.  d tau is accumulated as before.
+struct PurifiedMapTC : PurifiedMap {
+  __device__ __forceinline__ float grad(float raw, bool valid, float dp, float& g1, float& g2) const {
+    if (!valid) return 0.f;
+    float u = fmaxf(gamma * (raw - tau), 0.f);
+    float b = fmaxf(raw, 0.f);
+    float du = 4.f * (u * u * u) * dp;
+    g1 += eps_base * (b * b) * dp;
+    g2 += -du * gamma;
+    return du * gamma + 2.f * eps_base * b * dp;
+  }
+};
+
 __device__ __forceinline__ void set_status(int* status, int code, int site) {
   if (status != nullptr && atomicCAS(status, 0, code) == 0) status[1] = site;
 }
@@ -133,4 +164,8 @@ bool tc_bwd_supported(const Problem& p);
 int tc_bwd(const Problem& p, cudaStream_t s, int* launches);
 size_t tc_bwd_workspace(const Problem& p);
 void record_cuda_error(cudaError_t e);
+// TMA tensor maps (fb_tmap.cu)
+bool get_encoder();
+bool tma_ok(const Tensor4& t);
+bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows);
 }  // namespace fb

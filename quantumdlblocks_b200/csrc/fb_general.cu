@@ -16,8 +16,9 @@
 // In a row whose weight sits on one small overlap a, any rounding difference between the two
 // forms is amplified by ~2/a (Z ~ a^2); with fp32 O this alone exceeds 1e-4 in dQ at the C1
 // configuration.  This path therefore computes delta_i = sum_j w_ij (dO_i . v_j) from the same
-// recomputed dO.v products it later subtracts it from (a first pass of the dQ kernel), so the
-// cancellation is consistent; the dK/dV kernel reads it back.
+// recomputed dO.v products it later subtracts it from (a first pass of the dQ kernel), with its
+// own Z'_i = sum_j p_ij + eps recomputed in the same pass (so it does not depend on how the
+// forward rounded Z), and the cancellation is consistent; the dK/dV kernel reads both back.
 //   general_param_reduce    fixed-order sum of the partials into dscale/dtau (deterministic;
 //                           replaces the reference's atomic_add, :319-322)
 #include <algorithm>
@@ -43,6 +44,7 @@ struct GenArgs {
   const int32_t* doc;
   int64_t doc_s0, doc_s1;
   float* delta;     // B*H*T
+  float* zb;        // B*H*T: Z' recomputed by the backward
   float* partials;  // [B*H*n_kv_tiles][2]
   int n_kv_tiles;
 };
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(kThreads) general_bwd_kv_kernel(GenArgs a) {
     load_rows<T, KD>(dOs, a.dout, b, h, m0, BM, a.T, a.D);
     for (int r = tid; r < BM; r += kThreads) {
       int qi = m0 + r;
-      zq[r] = qi < a.T ? a.z[bh * a.T + qi] : 1.f;
+      zq[r] = qi < a.T ? a.zb[bh * a.T + qi] : 1.f;
       dq_[r] = qi < a.T ? a.delta[bh * a.T + qi] : 0.f;
       docq[r] = doc_at(a, b, qi);
     }
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(kThreads) general_bwd_q_kernel(GenArgs a) {
   load_rows<T, KD>(dOs, a.dout, b, h, m0, BM, a.T, a.D);
   for (int r = tid; r < BM; r += kThreads) {
     int qi = m0 + r;
-    zq[r] = qi < a.T ? a.z[bh * a.T + qi] : 1.f;
+    zq[r] = 1.f;  // replaced by Z' after pass 1
     dq_[r] = 0.f;
     docq[r] = doc_at(a, b, qi);
   }
@@ -381,8 +383,8 @@ __global__ void __launch_bounds__(kThreads) general_bwd_q_kernel(GenArgs a) {
     __syncthreads();
   };
 
-  // pass 1: delta_i = sum_j (p_ij / Z_i) (dO_i . v_j)
-  float dsum[2] = {0.f, 0.f};
+  // pass 1: Z'_i = sum_j p_ij + eps and delta_i = sum_j (p_ij / Z'_i) (dO_i . v_j)
+  float dsum[2] = {0.f, 0.f}, zsum[2] = {0.f, 0.f};
   for (int n0 = lo; n0 < hi; n0 += BN) {
     load_keys(n0);
     float s[2][2], dp[2][2];
@@ -393,21 +395,34 @@ __global__ void __launch_bounds__(kThreads) general_bwd_q_kernel(GenArgs a) {
       for (int y = 0; y < 2; ++y) {
         int qi = m0 + pm + x, kj = n0 + pn + y;
         bool valid = qi < a.T && pair_valid(qi, kj, a.T, a.causal, a.window, docq[pm + x], dock[pn + y]);
-        dsum[x] += map.prob(s[x][y], valid) * dp[x][y];
+        const float pv = map.prob(s[x][y], valid);
+        dsum[x] += pv * dp[x][y];
+        zsum[x] += pv;
       }
   }
 #pragma unroll
   for (int x = 0; x < 2; ++x) {
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) dsum[x] += __shfl_xor_sync(0xffffffffu, dsum[x], o);
+    for (int o = 8; o > 0; o >>= 1) {
+      dsum[x] += __shfl_xor_sync(0xffffffffu, dsum[x], o);
+      zsum[x] += __shfl_xor_sync(0xffffffffu, zsum[x], o);
+    }
   }
+  __syncthreads();
   if ((tid & 15) == 0) {
-    dq_[pm] = dsum[0] / zq[pm];
-    dq_[pm + 1] = dsum[1] / zq[pm + 1];
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const float zz = zsum[x] + a.eps;
+      zq[pm + x] = zz;
+      dq_[pm + x] = dsum[x] / zz;
+    }
   }
   __syncthreads();
   for (int r = tid; r < BM; r += kThreads)
-    if (m0 + r < a.T) a.delta[bh * a.T + m0 + r] = dq_[r];
+    if (m0 + r < a.T) {
+      a.delta[bh * a.T + m0 + r] = dq_[r];
+      a.zb[bh * a.T + m0 + r] = zq[r];
+    }
 
   // pass 2: dQ = sum_j dL/draw_ij k_j
   float dqa[KD / 8];
@@ -578,7 +593,7 @@ size_t general_bwd_workspace(const Problem& p) {
   const size_t n_kv = (size_t)((p.T + 31) / 32);
   size_t delta = (size_t)p.B * p.H * p.T * sizeof(float);
   delta = (delta + 255) & ~(size_t)255;
-  return delta + (size_t)p.B * p.H * n_kv * 2 * sizeof(float);
+  return 2 * delta + (size_t)p.B * p.H * n_kv * 2 * sizeof(float);
 }
 
 int general_bwd(const Problem& p, cudaStream_t s, int* launches) {
@@ -586,7 +601,8 @@ int general_bwd(const Problem& p, cudaStream_t s, int* launches) {
   size_t delta = (size_t)p.B * p.H * p.T * sizeof(float);
   delta = (delta + 255) & ~(size_t)255;
   a.delta = reinterpret_cast<float*>(p.ws);
-  a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + delta);
+  a.zb = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + delta);
+  a.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ws) + 2 * delta);
   a.n_kv_tiles = (p.T + 31) / 32;
   return p.purified ? bwd_dispatch<PurifiedMap>(a, p, s, launches) : bwd_dispatch<PlainMap>(a, p, s, launches);
 }

@@ -17,14 +17,14 @@
 //               P = bf16(p) -> tcgen05.st into P[j%2].  No exp, no running max, no rescale of O:
 //               the epilogue reads O once, divides by Z = sum p + eps and stores O and Z.
 //
-// Numerics follow the reference kernel (flash_born.py:156-191): S and O accumulate in fp32, Z sums
-// the fp32 p, PV consumes p rounded to bf16.
+// Numerics: S and O accumulate in fp32 and PV consumes p rounded to bf16, as in the reference
+// kernel (flash_born.py:156-191).  Z sums the same bf16-rounded p that PV consumes (the reference
+// sums the unrounded p), so O is an exact convex combination of the v rows: a row with a single
+// valid key returns that key's v exactly, and the backward's delta = dO.O cancels against dO.v
+// without the bf16 rounding of p (which the 2/a factor of dS would otherwise amplify).
 //
 // TMEM columns (512 allocated): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D).
 #include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
 
 #include "fb_common.cuh"
 #include "fb_sm100.cuh"
@@ -275,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 32; e += 2) {
             const float p0 = map.prob(__uint_as_float(r[e]), true);
             const float p1 = map.prob(__uint_as_float(r[e + 1]), true);
-            zsum += p0 + p1;
             w[e / 2] = pack2<true>(p0, p1);
+            zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
           }
         } else {
           const int kbase = n0 + c * 32;
@@ -291,8 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
               pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
             }
-            zsum += pr[0] + pr[1];
             w[e / 2] = pack2<true>(pr[0], pr[1]);
+            zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
           }
         }
         tmem_st16(lane_addr + Cfg::kTmemP + sb * (kBN / 2) + c * 16, w);
@@ -344,40 +344,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-std::once_flag g_encode_once;
-
-bool get_encoder() {
-  std::call_once(g_encode_once, [] {
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  });
-  return g_encode != nullptr;
-}
-
-// 4-D map over a (B, H, T, D) bf16 tensor: dims (D, T, H, B), box (64, 128, 1, 1), 128-B swizzle.
-bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D) {
-  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)t.s[2] * 2, (cuuint64_t)t.s[1] * 2, (cuuint64_t)t.s[0] * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)kBN, 1, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t.ptr), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-bool tma_ok(const Tensor4& t) {
-  if ((reinterpret_cast<uintptr_t>(t.ptr) & 15) != 0) return false;
-  if (t.s[3] != 1) return false;
-  for (int i = 0; i < 3; ++i)
-    if (t.s[i] % 8 != 0 || t.s[i] <= 0) return false;
-  return true;
-}
-
 template <int D, class Map, bool kHasDoc, typename TO>
 int launch_fwd(const Problem& pr, cudaStream_t s, const FwdParams& fp, const CUtensorMap& mq, const CUtensorMap& mk,
                const CUtensorMap& mv) {
@@ -420,8 +386,8 @@ bool tc_fwd_supported(const Problem& p) {
 int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (!get_encoder()) return FB_ERR_NO_DEVICE;
   CUtensorMap mq, mk, mv;
-  if (!encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D) || !encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D) ||
-      !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D))
+  if (!encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D, kBM) || !encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D, kBN) ||
+      !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D, kBN))
     return FB_ERR_ALIGN;
   FwdParams fp{};
   fp.B = pr.B; fp.H = pr.H; fp.T = pr.T;

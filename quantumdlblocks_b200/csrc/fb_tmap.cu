@@ -1,0 +1,49 @@
+// fb_tmap.cu -- host-side TMA tensor maps over (B, H, T, D) bf16 tensors.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "fb_common.cuh"
+
+namespace fb {
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+}  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+bool get_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// TMA needs a 16-byte aligned base, unit inner stride and 16-byte multiples for the others.
+bool tma_ok(const Tensor4& t) {
+  if ((reinterpret_cast<uintptr_t>(t.ptr) & 15) != 0) return false;
+  if (t.s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t.s[i] % 8 != 0 || t.s[i] <= 0) return false;
+  return true;
+}
+
+// 4-D map: dims (D, T, H, B), box (64, box_rows, 1, 1), 128-byte swizzle.  Rows at or beyond T
+// read as zeros (per head, since T is its own dimension).
+bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows) {
+  if (!get_encoder()) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)t.s[2] * 2, (cuuint64_t)t.s[1] * 2, (cuuint64_t)t.s[0] * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t.ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace fb

@@ -177,7 +177,7 @@ def _born_fwd_fake(q, k, v, scale, tau, doc_ids, is_causal, eps, window_size, ep
 @torch.library.custom_op("flashborn_b200::born_bwd", mutates_args=())
 def _born_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
               z: torch.Tensor, scale: torch.Tensor, tau: Optional[torch.Tensor], doc_ids: Optional[torch.Tensor],
-              is_causal: bool, window_size: int, eps_base: float,
+              is_causal: bool, eps: float, window_size: int, eps_base: float,
               purified: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     dq = torch.empty_like(q, memory_format=torch.contiguous_format)
     dk = torch.empty_like(k, memory_format=torch.contiguous_format)
@@ -186,7 +186,7 @@ def _born_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
     dtau = torch.zeros(tau.numel() if (purified and tau is not None) else 0, dtype=torch.float32, device=q.device)
     lib = _lib.load()
     a = _lib.FbAttnArgs()
-    _fill_common(a, q, k, v, out, z, scale, tau if purified else None, doc_ids, is_causal, 0.0, window_size, eps_base)
+    _fill_common(a, q, k, v, out, z, scale, tau if purified else None, doc_ids, is_causal, eps, window_size, eps_base)
     a.dout, a.dout_stride = _ptr(dout), _strides(dout)
     a.dq, a.dq_stride = _ptr(dq), _strides(dq)
     a.dk, a.dk_stride = _ptr(dk), _strides(dk)
@@ -203,7 +203,7 @@ def _born_bwd(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Ten
 
 
 @_born_bwd.register_fake
-def _born_bwd_fake(dout, q, k, v, out, z, scale, tau, doc_ids, is_causal, window_size, eps_base, purified):
+def _born_bwd_fake(dout, q, k, v, out, z, scale, tau, doc_ids, is_causal, eps, window_size, eps_base, purified):
     n_tau = tau.numel() if (purified and tau is not None) else 0
     return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
             q.new_empty((scale.numel(),), dtype=torch.float32), q.new_empty((n_tau,), dtype=torch.float32))
@@ -214,6 +214,7 @@ def _setup_context(ctx, inputs, output):
     out, z = output
     ctx.save_for_backward(q, k, v, out, z, scale, tau, doc_ids)
     ctx.is_causal = is_causal
+    ctx.eps = eps
     ctx.window_size = window_size
     ctx.eps_base = eps_base
     ctx.purified = purified
@@ -223,7 +224,7 @@ def _backward(ctx, dout, dz):
     q, k, v, out, z, scale, tau, doc_ids = ctx.saved_tensors
     # the reference casts dO to the saved value dtype (flash_born.py:532)
     dout = _prep(dout.to(v.dtype))
-    dq, dk, dv, dscale, dtau = _born_bwd(dout, q, k, v, out, z, scale, tau, doc_ids, ctx.is_causal,
+    dq, dk, dv, dscale, dtau = _born_bwd(dout, q, k, v, out, z, scale, tau, doc_ids, ctx.is_causal, ctx.eps,
                                          ctx.window_size, ctx.eps_base, ctx.purified)
     dtau_out = dtau if (ctx.purified and tau is not None) else None
     return dq, dk, dv, dscale, dtau_out, None, None, None, None, None, None

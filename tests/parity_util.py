@@ -5,8 +5,9 @@ Gates (from the task's tolerance statement):
   gradients larger than 1 are held to the same relative resolution).
 * bf16 / fp16 inputs: max-rel error ``max |x - r| / max |r|`` <= 2e-2 per tensor, against the
   float64 oracle evaluated on the rounded inputs.
-* parameter gradients (dscale, dgamma, dtau): absolute, scaled by the size of the other grads,
-  since dscale is analytically ~0 for the plain op (it equals sum_i delta_i 2 eps / (scale Z_i)).
+* parameter gradients (dscale, dgamma, dtau): bf16/fp16 -- max-rel 2e-2 against their own size,
+  floored at 1e-2 of the dQ/dK scale (the plain dscale is analytically sum_i 2 eps delta_i /
+  (scale Z_i) ~ 0); fp32 -- absolute 1e-4 of the dQ/dK scale.
 * a tensor that is analytically zero (dQ/dK when every row has a single valid key: then
   dO.v_j - delta_i = 0 exactly) is compared against an absolute floor: the max-rel denominator
   is at least 1e-3 x max(|out|, |dV|) of the same problem.
@@ -111,8 +112,13 @@ def check_all(got, ref, lowp: bool, names=("out", "dq", "dk", "dv"), floor_rel: 
         else:
             fp32_gate(got[n], ref[n], n)
     gscale = max(1.0, float(np.abs(ref["dq"]).max()), float(np.abs(ref["dk"]).max()))
-    ptol = (2e-2 if lowp else 1e-4) * gscale
     for n in ("dscale", "dtau"):
         if n in ref:
             err = float(np.abs(got[n].reshape(ref[n].shape) - ref[n]).max())
-            assert err <= ptol, f"{n}: {err:.3e} > {ptol:.3e}"
+            if lowp:
+                # max-rel against the parameter gradient's own size, floored for the plain dscale
+                # (analytically 2 eps sum delta / (scale Z) ~ 0) at 1e-2 of the dQ/dK scale
+                bound = LOWP_REL * max(float(np.abs(ref[n]).max()), 1e-2 * gscale)
+            else:
+                bound = FP32_ABS * gscale
+            assert err <= bound, f"{n}: {err:.3e} > {bound:.3e}"

@@ -81,9 +81,10 @@ def test_tc_forward_matches_oracle_and_general(case, purified):
     o_tc_np = o_tc.double().cpu().numpy()
     lowp_gate(o_tc_np, ref, "out(tcgen05)")
     lowp_gate(o_ge.double().cpu().numpy(), ref, "out(general)")
-    # Z: fp32 sums of the same fp32 p (only accumulation order differs)
-    np.testing.assert_allclose(z_tc.double().cpu().numpy(), zref, rtol=2e-3, atol=1e-30)
-    np.testing.assert_allclose(z_tc.cpu().numpy(), z_ge.cpu().numpy(), rtol=2e-3)
+    # Z (saved for the backward, not returned): the tensor-core forward sums the bf16-rounded p that
+    # its PV product consumes, so each term carries up to 2^-9 relative rounding
+    np.testing.assert_allclose(z_tc.double().cpu().numpy(), zref, rtol=5e-3, atol=1e-30)
+    np.testing.assert_allclose(z_tc.cpu().numpy(), z_ge.cpu().numpy(), rtol=5e-3)
 
 
 def test_tc_forward_is_selected_for_bf16_d64_d128():
@@ -105,3 +106,39 @@ def test_tc_forward_is_selected_for_bf16_d64_d128():
     assert _lib.load().fb_select_path(ctypes.byref(a), 0) == _lib.FB_PATH_TCGEN05
     a.dtype = a.out_dtype = _lib.FB_F16
     assert _lib.load().fb_select_path(ctypes.byref(a), 0) == _lib.FB_PATH_GENERAL
+
+
+BWD_CASES = [c for c in CASES if c[3] == 64]
+
+
+@pytest.mark.parametrize("purified", [False, True])
+@pytest.mark.parametrize("case", BWD_CASES, ids=[str(c) for c in BWD_CASES])
+def test_tc_backward_matches_oracle(case, purified):
+    """Forward and backward both forced onto the tcgen05 kernels (d=64), against the oracle."""
+    from parity_util import check_all, run_cuda, run_oracle
+
+    B, H, T, D, causal, window, doc_mean = case
+    rng = np.random.default_rng(B * 11 + T + D)
+    q, k, v, do = (rng.standard_normal((B, H, T, D)) for _ in range(4))
+    if purified:
+        q /= np.linalg.norm(q, axis=-1, keepdims=True)
+        k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    q, k, v, do = (round_to(x, torch.bfloat16) for x in (q, k, v, do))
+    doc = None
+    if doc_mean is not None:
+        doc = np.zeros((B, T), np.int32)
+        for b in range(B):
+            t, d = 0, 0
+            while t < T:
+                L = int(rng.geometric(1 / doc_mean))
+                doc[b, t:t + L] = d
+                t, d = t + L, d + 1
+    scale = np.linspace(6.0, 9.0, H).astype(np.float32) if purified else np.linspace(0.3, 0.5, H).astype(np.float32)
+    kw = dict(is_causal=causal, window_size=window, doc_ids=doc)
+    if purified:
+        kw["tau"] = np.linspace(0.02, 0.08, H).astype(np.float32)
+    got = run_cuda("purified" if purified else "plain", q, k, v, do, scale, dtype=torch.bfloat16, path="tcgen05",
+                   **kw)
+    assert fbm.device_status() == (0, 0)
+    ref = run_oracle("purified" if purified else "plain", q, k, v, do, scale, **kw)
+    check_all(got, ref, lowp=True)
