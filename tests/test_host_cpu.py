@@ -51,3 +51,26 @@ def test_kernel_path_override():
         fbm.set_kernel_path("auto")
     with pytest.raises(ValueError):
         fbm.set_kernel_path("triton")
+
+
+def test_swap_rebinds_reference_names_and_restores_them(monkeypatch):
+    """install() patches every module attribute the reference binds the kernels to."""
+    import sys
+    import types
+
+    from quantumdlblocks_b200 import swap
+
+    orig = object()
+    fake = {}
+    for modname, names in swap.TARGETS.items():
+        m = types.ModuleType(modname)
+        for n in names:
+            setattr(m, n, orig)
+        fake[modname] = m
+        monkeypatch.setitem(sys.modules, modname, m)
+    patched = swap.install(import_missing=False)
+    assert len(patched) == sum(len(v) for v in swap.TARGETS.values())
+    assert sys.modules["qdlblocks.layers.attention"].flash_born_attention is fbk.flash_born_attention
+    assert sys.modules["qdlblocks.kernels.flash_born"]._run_triton_flash_born is fbm._run_triton_flash_born
+    swap.uninstall()
+    assert all(getattr(fake[m], n) is orig for m, ns in swap.TARGETS.items() for n in ns)
