@@ -62,7 +62,8 @@ enum {
   FB_ERR_TIMEOUT = 6,     /* a bounded device-side wait gave up (device status word) */
   FB_ERR_WORKSPACE = 7,   /* workspace missing or too small */
   FB_ERR_NO_DEVICE = 8,   /* no CUDA device / driver entry point unavailable */
-  FB_ERR_UNSUPPORTED = 9  /* no kernel for this configuration (forced path not applicable) */
+  FB_ERR_UNSUPPORTED = 9, /* no kernel for this configuration (forced path not applicable) */
+  FB_ERR_SCRATCH_LIMIT = 10 /* fb_born_bwd_static_scratch: backward needs more than its static scratch */
 };
 
 /* Element types. */
@@ -125,6 +126,18 @@ FB_API int fb_purified_born_fwd(const fb_attn_args* args, void* stream);
 /* Purified backward: dq, dk, dv; accumulates dscale (d gamma) and dtau.
  * Replaces flash_born.py:1197-1262. */
 FB_API int fb_purified_born_bwd(const fb_attn_args* args, void* stream);
+
+/* Plain flash-Born backward that allocates nothing and takes no workspace: its scratch is a
+ * fixed FB_STATIC_SCRATCH_BYTES device array inside the library (one per GPU, held from the
+ * first call on that GPU until exit).  For callers that cannot allocate device memory (a host
+ * runtime with no device allocator of its own, or a step that must not call cudaMalloc).
+ * Same arguments and results as fb_born_bwd except workspace/workspace_bytes, which it ignores.
+ * Returns FB_ERR_SCRATCH_LIMIT when fb_bwd_workspace_size() exceeds FB_STATIC_SCRATCH_BYTES.
+ * The first call on a device looks up the array's address there; make it before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the GPU race.
+ * No counterpart in the reference (its kernels allocate through PyTorch). */
+#define FB_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
+FB_API int fb_born_bwd_static_scratch(const fb_attn_args* args, void* stream);
 
 /* Bytes of device workspace the backward needs for these arguments (0 allowed for none).
  * A non-NULL tau marks purified arguments here and in fb_select_path.

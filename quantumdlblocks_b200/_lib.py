@@ -22,6 +22,8 @@ FB_ERR_TIMEOUT = 6
 FB_ERR_WORKSPACE = 7
 FB_ERR_NO_DEVICE = 8
 FB_ERR_UNSUPPORTED = 9
+FB_ERR_SCRATCH_LIMIT = 10
+FB_STATIC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 FB_F32, FB_F16, FB_BF16 = 0, 1, 2
 FB_PATH_AUTO, FB_PATH_TCGEN05, FB_PATH_GENERAL = 0, 1, 2
@@ -62,6 +64,7 @@ _PARGS = ctypes.POINTER(FbAttnArgs)
 SIGNATURES = {
     "fb_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_born_bwd_static_scratch": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_purified_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_purified_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_bwd_workspace_size": (ctypes.c_size_t, [_PARGS]),
@@ -94,6 +97,9 @@ def load() -> ctypes.CDLL:
                     "(the flash-Born op has no fallback path)")
             lib = ctypes.CDLL(LIB_PATH)
             for name, (res, argtypes) in SIGNATURES.items():
+                if not hasattr(lib, name):
+                    raise FlashBornLibraryError(f"{LIB_PATH} does not export {name}: rebuild it "
+                                                "(`python -m quantumdlblocks_b200.build`)")
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = argtypes
@@ -102,10 +108,11 @@ def load() -> ctypes.CDLL:
 
 
 def available() -> bool:
+    """True when the library loads and exports every declared entry point (a stale build does not)."""
     try:
         load()
         return True
-    except (OSError, FlashBornLibraryError):
+    except (OSError, AttributeError, FlashBornLibraryError):
         return False
 
 

@@ -217,6 +217,7 @@ const char* fb_strerror(int status) {
     case FB_ERR_WORKSPACE: return "flashborn: backward workspace missing or smaller than fb_bwd_workspace_size()";
     case FB_ERR_NO_DEVICE: return "flashborn: no usable CUDA device";
     case FB_ERR_UNSUPPORTED: return "flashborn: the forced tcgen05 path does not support this configuration";
+    case FB_ERR_SCRATCH_LIMIT: return "flashborn: this backward needs more scratch than the library's static array (FB_STATIC_SCRATCH_BYTES); call fb_born_bwd with a workspace instead";
     default: return "flashborn: unknown status";
   }
 }

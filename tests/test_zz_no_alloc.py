@@ -1,0 +1,91 @@
+"""fb_born_bwd_static_scratch: the backward entry point that allocates nothing.
+
+Some callers cannot allocate device memory -- a host runtime that binds only this library's C
+functions and has no device allocator, or a training step that must not call cudaMalloc (it can
+synchronise the device, and fails once another framework's pool holds the GPU).  They call
+fb_born_bwd_static_scratch, which takes no workspace and runs the backward out of a fixed device
+array inside the library.  These tests call it through the C ABI, twice in a row, and compare its
+gradients with fb_born_bwd given a caller-allocated workspace; and they check that a problem
+needing more scratch than the array holds is refused.  The file name makes pytest collect it last.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from quantumdlblocks_b200 import _lib
+from quantumdlblocks_b200.kernels import flash_born as fbm
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("CUDA device required", allow_module_level=True)
+
+MAX_REL = 2e-2  # the bf16 gate used by every other parity test
+
+
+def _problem(dtype, B=2, H=4, T=640, D=64, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v, do = (torch.randn(B, H, T, D, generator=g).to(dtype).cuda() for _ in range(4))
+    scale = torch.linspace(0.3, 0.5, H).cuda()
+    out, z = torch.ops.flashborn_b200.born_fwd(q, k, v, scale, None, None, True, 1e-12, 0, 0.0, False)
+    return dict(q=q, k=k, v=v, do=do, scale=scale, out=out, z=z)
+
+
+def _args(p, dq, dk, dv, dscale, workspace=None):
+    a = _lib.FbAttnArgs()
+    fbm._fill_common(a, p["q"], p["k"], p["v"], p["out"], p["z"], p["scale"], None, None, True, 1e-12, 0, 0.0)
+    a.dout, a.dout_stride = p["do"].data_ptr(), _lib._I64x4(*p["do"].stride())
+    a.dq, a.dq_stride = dq.data_ptr(), _lib._I64x4(*dq.stride())
+    a.dk, a.dk_stride = dk.data_ptr(), _lib._I64x4(*dk.stride())
+    a.dv, a.dv_stride = dv.data_ptr(), _lib._I64x4(*dv.stride())
+    a.dscale = dscale.data_ptr()
+    if workspace is not None:
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    return a
+
+
+def _grads(p, fn, with_workspace):
+    lib = _lib.load()
+    dq, dk, dv = (torch.empty_like(p["q"]) for _ in range(3))
+    dscale = torch.zeros(p["scale"].numel(), device="cuda")
+    a = _args(p, dq, dk, dv, dscale)
+    if with_workspace:
+        ws = torch.empty(int(lib.fb_bwd_workspace_size(ctypes.byref(a))), dtype=torch.uint8, device="cuda")
+        a = _args(p, dq, dk, dv, dscale, ws)
+    rc = fn(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == _lib.FB_OK, lib.fb_strerror(rc).decode()
+    return [t.double().cpu().numpy() for t in (dq, dk, dv, dscale)]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_static_scratch_backward_matches_workspace_backward(dtype):
+    lib = _lib.load()
+    p = _problem(dtype)
+    ref = _grads(p, lib.fb_born_bwd, with_workspace=True)
+    scale_of_grads = max(float(np.abs(ref[0]).max()), float(np.abs(ref[1]).max()), 1.0)
+    for call in range(2):  # the array keeps the previous call's contents; both calls must be right
+        got = _grads(p, lib.fb_born_bwd_static_scratch, with_workspace=False)
+        for name, x, r in zip(("dq", "dk", "dv"), got[:3], ref[:3]):
+            err = float(np.abs(x - r).max() / max(np.abs(r).max(), 1e-30))
+            assert err <= MAX_REL, f"call {call} {name}: max-rel {err:.3e}"
+        assert float(np.abs(got[3] - ref[3]).max()) <= MAX_REL * 1e-2 * scale_of_grads, f"call {call} dscale"
+    assert fbm.device_status() == (0, 0)
+
+
+def test_static_scratch_refuses_problems_over_the_limit():
+    lib = _lib.load()
+    p = _problem(torch.bfloat16, B=1, H=1, T=128)
+    dq, dk, dv = (torch.empty_like(p["q"]) for _ in range(3))
+    dscale = torch.zeros(1, device="cuda")
+    a = _args(p, dq, dk, dv, dscale)
+    # claim a C2-sized problem: its backward needs ~70 MB of scratch; refused before any launch
+    a.batch, a.heads, a.seq_len = 8, 16, 2048
+    assert lib.fb_bwd_workspace_size(ctypes.byref(a)) > _lib.FB_STATIC_SCRATCH_BYTES
+    rc = lib.fb_born_bwd_static_scratch(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.FB_ERR_SCRATCH_LIMIT
+    assert "static" in lib.fb_strerror(rc).decode()
