@@ -10,7 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/flashborn_b200.h"
+#include "flashborn_b200.h"  // -I include
 
 namespace fb {
 
@@ -168,4 +168,5 @@ void record_cuda_error(cudaError_t e);
 bool get_encoder();
 bool tma_ok(const Tensor4& t);
 bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows);
+bool encode_rows_f32(CUtensorMap* m, float* base, int64_t rows);
 }  // namespace fb

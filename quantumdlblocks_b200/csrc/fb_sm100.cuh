@@ -21,6 +21,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Dynamic shared memory rounded up to a 1024-byte boundary (128-byte swizzle atoms) by pointer
+// arithmetic on the shared array itself, so the compiler keeps the shared address space and
+// emits shared-memory instructions for every access derived from it.
+__device__ __forceinline__ uint8_t* smem_align1024(uint8_t* raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -126,6 +133,13 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src,
   asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
                    reinterpret_cast<uint64_t>(dst)),
                "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+// 2-D tiled bulk reduction shared -> global through a tensor map: tile += smem box (fp32 add)
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }

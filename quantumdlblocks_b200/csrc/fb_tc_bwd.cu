@@ -1,11 +1,11 @@
 // fb_tc_bwd.cu -- flash-Born backward on the tcgen05 tensor cores (sm_100a), head dim 64.
 //
 // Three launches (all on the caller's stream):
-//   1. bwd_prep_kernel   delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded to a multiple of
-//                        64), and a zeroed fp32 dQ accumulator            (workspace)
+//   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
+//                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
 //   2. tc_bwd_kernel     one CTA per (batch, head, 128-key tile); walks the 64-query tiles that
 //                        can hold valid pairs and accumulates dK, dV in TMEM; dQ partials are
-//                        reduced into the fp32 accumulator with TMA bulk reduce-add
+//                        reduced into the fp32 accumulator with TMA tensor reduce-add
 //   3. bwd_post_kernel   dQ = accumulator -> input dtype
 //   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
 //                        sums and the main kernel's per-CTA partials
@@ -21,8 +21,10 @@
 //   dK  += G^T Q        same                              A=G^T (TMEM), B=Q (smem MN-major)
 //   dQ_t = G K          M=64 queries, N=64, K=128 keys    A=G (smem MN-major), B=K (smem MN-major)
 //
-// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 pointwise (key rows),
-// 6-9 dQ epilogue (TMEM -> smem -> bulk reduce-add).  S^T/dP^T/dQ are double-buffered in TMEM so
+// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-9 two pointwise warpgroups
+// (key rows; group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two
+// groups' latency chains interleave).  Before each tile a group drains the dQ partial of its
+// previous tile (TMEM -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator).  S^T/dP^T/dQ are double-buffered in TMEM so
 // the products of query tile t+1 overlap the pointwise work of tile t.
 //
 // TMEM columns: S^T[0..1] 0/64, dP^T[0..1] 128/192, dV 256, dK 320, dQ[0..1] 384/448.
@@ -49,9 +51,9 @@ constexpr uint32_t kSV = 16384;                // V tile                    16 K
 constexpr uint32_t kSQ = 32768;                // Q stages [2] 64 x 64       8 KB each
 constexpr uint32_t kSdO = 49152;               // dO stages [2]              8 KB each
 constexpr uint32_t kSG = 65536;                // G [2] 128 keys x 64 q      16 KB each
-constexpr uint32_t kSStg = 98304;              // dQ staging [4 warps][2] 16 rows x 256 B
-constexpr uint32_t kSVec = 131072;             // delta[2][64], zinv[2][64] fp32
-constexpr uint32_t kSDoc = kSVec + 1024;       // query doc ids [4 warps][2][64] int32
+constexpr uint32_t kSStg = 98304;              // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
+constexpr uint32_t kSVec = 131072;             // dlz[2][64] (delta / Z), zinv[2][64] (1 / Z) fp32
+constexpr uint32_t kSDoc = kSVec + 1024;       // query doc ids [8 warps][64] int32
 constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
 constexpr uint32_t kSmemBytes = kSBar + 256;
 
@@ -69,8 +71,8 @@ struct BwdParams {
   int64_t dk_s0, dk_s1, dk_s2;
   __nv_bfloat16* dv;
   int64_t dv_s0, dv_s1, dv_s2;
-  const float* delta;  // [BH][Tpad]
-  const float* zinv;   // [BH][Tpad]
+  const float* dlz;    // [BH][Tpad]  delta_i / Z_i
+  const float* zinv;   // [BH][Tpad]  1 / Z_i
   float* dq_acc;       // [BH][Tpad][64]
   float* partials;     // [BH][n_kv][2]
   int n_kv;
@@ -109,9 +111,9 @@ template <class Map, bool kHasDoc>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
-                  const BwdParams p) {
+                  const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
   uint64_t* kv_full = bars + 0;
   uint64_t* q_full = bars + 1;     // [2]
@@ -125,8 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
-  float* red = reinterpret_cast<float*>(bars + 19);  // [4 warps][2]
-  float* vdelta = reinterpret_cast<float*>(smem + kSVec);        // [2][64]
+  float* red = reinterpret_cast<float*>(bars + 19);  // [8 pointwise warps][2]
+  float* vdlz = reinterpret_cast<float*>(smem + kSVec);          // [2][64]
   float* vzinv = reinterpret_cast<float*>(smem + kSVec + 512);   // [2][64]
 
   const int warp = threadIdx.x >> 5;
@@ -160,6 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmV);
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmdO);
+    prefetch_tensormap(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&q_full[st], 2 * kBM * kD * 2 + 2 * kBM * 4);
         tma_load_4d(smem + kSQ + st * 8192, &tmQ, &q_full[st], 0, m0, h, b);
         tma_load_4d(smem + kSdO + st * 8192, &tmdO, &q_full[st], 0, m0, h, b);
-        bulk_load(vdelta + st * kBM, p.delta + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
+        bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
         bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
         issued = t + 1;
       }
@@ -255,8 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ------------------------------------------------------------------ pointwise (key rows)
+    const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;
     const int jr = lg * 32 + lane;  // key row within the tile == TMEM lane
     const int kj = n0 + jr;
@@ -264,18 +268,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Map map = BwdMap<Map>::make(p, h);
     int doc_j = 0;
     if constexpr (kHasDoc) doc_j = kj < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
-    int* docq = reinterpret_cast<int*>(smem + kSDoc) + lg * 2 * kBM;
+    int* docq = reinterpret_cast<int*>(smem + kSDoc) + (wg * 4 + lg) * kBM;
     uint8_t* g_row0 = smem + kSG + jr * 128;
+    uint8_t* stg = smem + kSStg + lg * 8192 + wg * 4096;  // this warp's dQ staging (two 16 x 32 boxes)
+    const bool leader = elect_one();
     float g1 = 0.f, g2 = 0.f;
     bool ok = true;
-    for (int t = 0; t < n_tiles && ok; ++t) {
-      const int sb = t & 1;
+    // dQ partial of tile u (TMEM buffer wg; an M=64 accumulator keeps rows 16lg..16lg+15 in lanes
+    // 0..15 of this warp's quadrant) -> swizzled staging -> TMA reduce-add into the accumulator
+    auto drain_dq = [&](int u) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[wg], (u >> 1) & 1, wc, 29))) return false;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      tmem_ld32(lane_addr + kTdQ + wg * kD, r0);
+      tmem_ld32(lane_addr + kTdQ + wg * kD + 32, r1);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&dq_empty[wg]);
+      if (leader) bulk_wait_read<0>();  // the previous reduce from this staging buffer has read it
+      __syncwarp();
+      if (lane < 16) {
+        uint8_t* row0 = stg + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(row0 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(r0[4 * c]), __uint_as_float(r0[4 * c + 1]), __uint_as_float(r0[4 * c + 2]),
+                          __uint_as_float(r0[4 * c + 3]));
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(row0 + 2048 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(r1[4 * c]), __uint_as_float(r1[4 * c + 1]), __uint_as_float(r1[4 * c + 2]),
+                          __uint_as_float(r1[4 * c + 3]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (leader) {
+        const int grow = (int)(bh * p.Tpad + m_first + u * kBM + 16 * lg);
+        tma_reduce_add_2d(&tmDQ, stg, 0, grow);
+        tma_reduce_add_2d(&tmDQ, stg + 2048, 32, grow);
+        bulk_commit();
+      }
+      return true;
+    };
+    int t_prev = -1;
+    for (int t = wg; t < n_tiles && ok; t += 2) {
+      if (t_prev >= 0) {
+        ok = drain_dq(t_prev);
+        if (!ok) break;
+      }
+      t_prev = t;
+      const int sb = wg;  // == t & 1
       const int m0 = m_first + t * kBM;
       if constexpr (kHasDoc) {
 #pragma unroll
         for (int u = 0; u < kBM / 32; ++u) {
           const int qi = m0 + u * 32 + lane;
-          docq[sb * kBM + u * 32 + lane] = qi < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+          docq[u * 32 + lane] = qi < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
         }
         __syncwarp();
       }
@@ -285,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
                         (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
                         (n0 + kBN <= p.T);
-      const float* dl = vdelta + sb * kBM;
+      const float* dl = vdlz + sb * kBM;
       const float* zi = vzinv + sb * kBM;
       uint8_t* g_row = g_row0 + sb * 16384;
 #pragma unroll 1
@@ -293,6 +341,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t rs[32], rd[32];
         tmem_ld32(lane_addr + kTS + sb * kBM + c * 32, rs);
         tmem_ld32(lane_addr + kTdP + sb * kBM + c * 32, rd);
+        float zc[32], dc[32];  // per-query 1/Z and delta/Z of these 32 columns (shared, broadcast)
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4) {
+          const float4 z4 = reinterpret_cast<const float4*>(zi + c * 32)[v4];
+          const float4 d4 = reinterpret_cast<const float4*>(dl + c * 32)[v4];
+          zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
+          dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+        }
         tmem_wait_ld();
         uint32_t wpk[16], gpk[16];
 #pragma unroll
@@ -304,13 +360,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool valid = true;
             if (!full) {
               int doc_i = 0;
-              if constexpr (kHasDoc) doc_i = docq[sb * kBM + qx];
+              if constexpr (kHasDoc) doc_i = docq[qx];
               valid = pair_valid(m0 + qx, kj, p.T, p.causal, p.window, doc_i, doc_j);
             }
             const float raw = __uint_as_float(rs[e + u]);
-            const float zq = zi[qx];
-            wv[u] = map.prob(raw, valid) * zq;
-            gv[u] = map.grad(raw, valid, (__uint_as_float(rd[e + u]) - dl[qx]) * zq, g1, g2);
+            wv[u] = map.prob(raw, valid) * zc[e + u];
+            gv[u] = map.grad(raw, valid, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
           }
           wpk[e / 2] = pack2<true>(wv[0], wv[1]);
           gpk[e / 2] = pack2<true>(gv[0], gv[1]);
@@ -330,12 +385,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&wg_full[sb]);
     }
-    // dK, dV rows
+    if (ok && t_prev >= 0) ok = drain_dq(t_prev);
+    if (leader) bulk_wait<0>();  // every reduce has finished reading shared memory
+    __syncwarp();
+    // dK, dV rows: group 0 stores dV, group 1 stores dK
     if (ok) ok = __all_sync(0xffffffffu, n_tiles == 0 || mbar_wait(acc_full, 0, wc, 28));
     if (ok) {
       tc_fence_after();
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
+      {
+        const int which = wg;
         __nv_bfloat16* dst = which == 0 ? p.dv + (int64_t)b * p.dv_s0 + (int64_t)h * p.dv_s1 + (int64_t)kj * p.dv_s2
                                         : p.dk + (int64_t)b * p.dk_s0 + (int64_t)h * p.dk_s1 + (int64_t)kj * p.dk_s2;
 #pragma unroll 1
@@ -361,61 +419,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       g2 += __shfl_xor_sync(0xffffffffu, g2, o);
     }
     if (lane == 0) {
-      red[lg * 2] = g1;
-      red[lg * 2 + 1] = g2;
+      red[(wg * 4 + lg) * 2] = g1;
+      red[(wg * 4 + lg) * 2 + 1] = g2;
     }
-  } else {
-    // ------------------------------------------------------------------ dQ epilogue
-    const int qd = warp & 3;  // TMEM lane quadrant; an M=64 accumulator keeps rows 16qd..16qd+15 in lanes 0..15
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    uint8_t* stg0 = smem + kSStg + qd * 8192;
-    bool ok = true;
-    const bool leader = elect_one();
-    for (int t = 0; t < n_tiles && ok; ++t) {
-      const int su = t & 1;
-      const int m0 = m_first + t * kBM;
-      ok = __all_sync(0xffffffffu, mbar_wait(&dq_full[su], (t >> 1) & 1, wc, 29));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld32(lane_addr + kTdQ + su * kD, r0);
-      tmem_ld32(lane_addr + kTdQ + su * kD + 32, r1);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&dq_empty[su]);
-      uint8_t* stg = stg0 + su * 4096;
-      if (t >= 2) {
-        if (leader) bulk_wait_read<1>();  // the reduce issued from this buffer two tiles ago has read it
-        __syncwarp();
-      }
-      if (lane < 16) {
-        float4* row = reinterpret_cast<float4*>(stg + lane * 256);
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          row[v] = make_float4(__uint_as_float(r0[4 * v]), __uint_as_float(r0[4 * v + 1]), __uint_as_float(r0[4 * v + 2]),
-                               __uint_as_float(r0[4 * v + 3]));
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          row[8 + v] = make_float4(__uint_as_float(r1[4 * v]), __uint_as_float(r1[4 * v + 1]),
-                                   __uint_as_float(r1[4 * v + 2]), __uint_as_float(r1[4 * v + 3]));
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (leader) {
-        bulk_reduce_add_f32(p.dq_acc + ((bh * p.Tpad + m0 + 16 * qd) * kD), stg, 16 * kD * 4);
-        bulk_commit();
-      }
-    }
-    if (leader) bulk_wait<0>();
-    __syncwarp();
   }
 
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
     float* part = p.partials + (bh * p.n_kv + ktile) * 2;
-    part[0] = red[0] + red[2] + red[4] + red[6];
-    part[1] = red[1] + red[3] + red[5] + red[7];
+    float t1 = 0.f, t2 = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      t1 += red[2 * w];
+      t2 += red[2 * w + 1];
+    }
+    part[0] = t1;
+    part[1] = t2;
   }
   if (warp == 1) {
     tc_fence_after();
@@ -438,7 +457,7 @@ struct AuxParams {
   const __nv_bfloat16* dout;
   int64_t do_s0, do_s1, do_s2, do_s3;
   const float* z;
-  float* delta;
+  float* dlz;
   float* zinv;
   float* dq_acc;
   __nv_bfloat16* dq;
@@ -450,38 +469,47 @@ struct AuxParams {
   int scale_per_head, tau_per_head;
 };
 
-// One block per (64-row chunk, head, batch); each warp handles 8 rows: delta, 1/Z, a zeroed
-// dQ accumulator row, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of dscale /
-// d gamma).
+// One block per (64-row chunk, head, batch); each warp handles 8 rows: delta_i / Z_i, 1 / Z_i,
+// a zeroed dQ accumulator row, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
+// dscale / d gamma).
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t bh = (int64_t)b * a.H + h;
   __shared__ float csum_w[8];
   float csum = 0.f;
+#pragma unroll 4
   for (int r = 0; r < 8; ++r) {
     const int i = chunk * 64 + warp * 8 + r;
     const int64_t row = bh * a.Tpad + i;
     float s = 0.f;
     if (i < a.T) {
-      for (int d = lane; d < a.D; d += 32) {
+      for (int d = 2 * lane; d < a.D; d += 64) {  // two adjacent elements per lane
         const int64_t oo = (int64_t)b * a.o_s0 + (int64_t)h * a.o_s1 + (int64_t)i * a.o_s2 + (int64_t)d * a.o_s3;
-        const float o = a.out_f32 ? reinterpret_cast<const float*>(a.out)[oo]
-                                  : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.out)[oo]);
-        s += o * __bfloat162float(a.dout[(int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 +
-                                         (int64_t)d * a.do_s3]);
+        const int64_t od = (int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 + (int64_t)d * a.do_s3;
+        float o0, o1;
+        if (a.out_f32) {
+          const float* op = reinterpret_cast<const float*>(a.out) + oo;
+          o0 = op[0];
+          o1 = op[a.o_s3];
+        } else {
+          const __nv_bfloat16* op = reinterpret_cast<const __nv_bfloat16*>(a.out) + oo;
+          o0 = __bfloat162float(op[0]);
+          o1 = __bfloat162float(op[a.o_s3]);
+        }
+        s += o0 * __bfloat162float(a.dout[od]) + o1 * __bfloat162float(a.dout[od + a.do_s3]);
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     if (lane == 0) {
       const float zi = i < a.T ? 1.f / a.z[bh * a.T + i] : 0.f;
-      a.delta[row] = s;
+      a.dlz[row] = s * zi;
       a.zinv[row] = zi;
       csum += a.eps * s * zi;
     }
-    float* acc = a.dq_acc + row * a.D;
-    for (int d = lane; d < a.D; d += 32) acc[d] = 0.f;
+    float2* acc = reinterpret_cast<float2*>(a.dq_acc + row * a.D);
+    for (int d = lane; d < a.D / 2; d += 32) acc[d] = make_float2(0.f, 0.f);
   }
   if (lane == 0) csum_w[warp] = csum;
   __syncthreads();
@@ -557,7 +585,7 @@ __global__ void bwd_param_kernel(const AuxParams a) {
 }
 
 struct WsLayout {
-  size_t delta, zinv, dq_acc, partials, prep_part, total;
+  size_t dlz, zinv, dq_acc, partials, prep_part, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -567,8 +595,8 @@ WsLayout ws_layout(const Problem& p) {
   const size_t BH = (size_t)p.B * p.H;
   const int n_kv = (p.T + kBN - 1) / kBN;
   WsLayout w;
-  w.delta = 0;
-  w.zinv = align256(w.delta + BH * Tpad * 4);
+  w.dlz = 0;
+  w.zinv = align256(w.dlz + BH * Tpad * 4);
   w.dq_acc = align256(w.zinv + BH * Tpad * 4);
   w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
   w.prep_part = align256(w.partials + BH * n_kv * 2 * 4);
@@ -585,13 +613,13 @@ bool rows16(const Tensor4& t) {  // 16-byte vector row stores of bf16 rows
 
 template <class Map, bool kHasDoc>
 int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp, const CUtensorMap& mk, const CUtensorMap& mv,
-                const CUtensorMap& mq, const CUtensorMap& mdo) {
+                const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mdq) {
   auto kernel = tc_bwd_kernel<Map, kHasDoc>;
   const uint32_t smem = kSmemBytes + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   dim3 grid(bp.n_kv, pr.H, pr.B);
-  kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, bp);
+  kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, mdq, bp);
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   return FB_OK;
@@ -632,7 +660,7 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   a.dout = static_cast<const __nv_bfloat16*>(pr.dout.ptr);
   a.do_s0 = pr.dout.s[0]; a.do_s1 = pr.dout.s[1]; a.do_s2 = pr.dout.s[2]; a.do_s3 = pr.dout.s[3];
   a.z = pr.z;
-  a.delta = reinterpret_cast<float*>(ws + w.delta);
+  a.dlz = reinterpret_cast<float*>(ws + w.dlz);
   a.zinv = reinterpret_cast<float*>(ws + w.zinv);
   a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
   a.dq = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dq.ptr));
@@ -654,21 +682,23 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   bp.dk_s0 = pr.dk.s[0]; bp.dk_s1 = pr.dk.s[1]; bp.dk_s2 = pr.dk.s[2];
   bp.dv = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dv.ptr));
   bp.dv_s0 = pr.dv.s[0]; bp.dv_s1 = pr.dv.s[1]; bp.dv_s2 = pr.dv.s[2];
-  bp.delta = a.delta; bp.zinv = a.zinv; bp.dq_acc = a.dq_acc;
+  bp.dlz = a.dlz; bp.zinv = a.zinv; bp.dq_acc = a.dq_acc;
   bp.partials = reinterpret_cast<float*>(ws + w.partials);
   bp.n_kv = n_kv;
   bp.status = pr.status;
 
+  CUtensorMap mdq;
+  if (!encode_rows_f32(&mdq, a.dq_acc, (int64_t)pr.B * pr.H * Tpad)) return FB_ERR_ALIGN;
   bwd_prep_kernel<<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   int rc;
   if (pr.purified)
-    rc = pr.doc ? launch_main<PurifiedMapTC, true>(pr, s, bp, mk, mv, mq, mdo)
-                : launch_main<PurifiedMapTC, false>(pr, s, bp, mk, mv, mq, mdo);
+    rc = pr.doc ? launch_main<PurifiedMapTC, true>(pr, s, bp, mk, mv, mq, mdo, mdq)
+                : launch_main<PurifiedMapTC, false>(pr, s, bp, mk, mv, mq, mdo, mdq);
   else
-    rc = pr.doc ? launch_main<PlainMapNoParam, true>(pr, s, bp, mk, mv, mq, mdo)
-                : launch_main<PlainMapNoParam, false>(pr, s, bp, mk, mv, mq, mdo);
+    rc = pr.doc ? launch_main<PlainMapNoParam, true>(pr, s, bp, mk, mv, mq, mdo, mdq)
+                : launch_main<PlainMapNoParam, false>(pr, s, bp, mk, mv, mq, mdo, mdq);
   if (rc != FB_OK) return rc;
   const int64_t post_threads = (int64_t)pr.B * pr.H * pr.T * (pr.D / 8);
   bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);

@@ -2,7 +2,7 @@
 //
 // One CTA owns a tile of 128 queries of one (batch, head) and walks the key tiles (128 keys)
 // that can hold valid pairs (causal / window tile skipping, as flash_born.py:152-156).
-// Warp-specialised pipeline (192 threads):
+// Warp-specialised pipeline (320 threads):
 //
 //   warp 0      TMA producer: Q tile once, then K_j / V_j through an smem ring of kStages stages
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
@@ -12,10 +12,12 @@
 //                                    D = O in TMEM (fp32)
 //               S_{j+1} is issued before O += P_j V_j so the tensor core works while the
 //               pointwise warps turn S_j into P_j.
-//   warps 2-5   pointwise ("Born") warpgroup: thread r owns TMEM lane r = query row r.
+//   warps 2-9   two pointwise ("Born") warpgroups; group g handles key tiles j with j % 2 == g
+//               (TMEM buffers S[g], P[g]); thread r of a group owns TMEM lane r = query row r.
 //               tcgen05.ld S row -> a = relu(scale s) (masked), p = a^2, Z += p (fp32),
-//               P = bf16(p) -> tcgen05.st into P[j%2].  No exp, no running max, no rescale of O:
-//               the epilogue reads O once, divides by Z = sum p + eps and stores O and Z.
+//               P = bf16(p) -> tcgen05.st into P[g].  No exp, no running max, no rescale of O:
+//               the epilogue adds the two groups' row sums, reads O once, divides by
+//               Z = sum p + eps and stores O (each group half the columns) and Z.
 //
 // Numerics: S and O accumulate in fp32 and PV consumes p rounded to bf16, as in the reference
 // kernel (flash_born.py:156-191).  Z sums the same bf16-rounded p that PV consumes (the reference
@@ -36,7 +38,7 @@ using namespace sm100;
 
 constexpr int kBM = 128;      // queries per CTA (one M=128 MMA)
 constexpr int kBN = 128;      // keys per tile
-constexpr int kThreads = 192; // 6 warps
+constexpr int kThreads = 320; // 10 warps
 constexpr uint32_t kTmemCols = 512;
 
 template <int D>
@@ -49,8 +51,9 @@ struct FwdCfg {
   static constexpr uint32_t kKOff = kTileBytes;
   static constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
   static constexpr uint32_t kBarOff = kVOff + kStages * kTileBytes;
-  static constexpr uint32_t kDocOff = kBarOff + 256;             // [4 warps][2][kBN] int32
-  static constexpr uint32_t kSmemBytes = kDocOff + 4 * 2 * kBN * 4;
+  static constexpr uint32_t kDocOff = kBarOff + 256;             // [8 warps][kBN] int32
+  static constexpr uint32_t kZOff = kDocOff + 8 * kBN * 4;         // [2 groups][kBM] fp32 row sums
+  static constexpr uint32_t kSmemBytes = kZOff + 2 * kBM * 4;
   static constexpr uint32_t kTmemS = 0, kTmemP = 256, kTmemO = 384;
 };
 
@@ -98,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;             // [S]
@@ -108,9 +111,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pv_done = bars + 5 + 2 * S;     // [2]
   uint64_t* o_full = bars + 7 + 2 * S;
   uint64_t* drain = bars + 8 + 2 * S;
+  uint64_t* z_bar = bars + 9 + 2 * S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
-  int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);  // per pointwise warp: [2][kBN]
+  int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);  // per pointwise warp: [kBN]
+  float* zpart = reinterpret_cast<float*>(smem + Cfg::kZOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -134,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
+    mbar_init(z_bar, 256);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -230,57 +236,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------------ pointwise warpgroup
+    // ------------------------------------------------------------------ pointwise warpgroups
+    // Warpgroup g (warps 2+4g .. 5+4g) turns the S tiles j with j % 2 == g into P, so it always
+    // uses TMEM buffer S[g]/P[g]; the two groups' TMEM latency chains interleave on the SM.
+    const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;              // TMEM lane group of this warp
     const int row = lg * 32 + lane;       // query row within the tile == TMEM lane
     const int qi = m0 + row;
-    int* docs_k = docs_all + lg * 2 * kBN;  // this warp's copy of the key tile's doc ids
+    int* docs_k = docs_all + (wg * 4 + lg) * kBN;  // this warp's copy of the key tile's doc ids
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    const uint32_t s_addr = lane_addr + Cfg::kTmemS + wg * kBN;
+    const uint32_t p_addr = lane_addr + Cfg::kTmemP + wg * (kBN / 2);
     const Map map = TcMap<Map>::make(p, h);
     int doc_i = 0;
     if constexpr (kHasDoc) doc_i = qi < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
     float zsum = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_count && ok; ++j) {
+    for (int j = wg; j < n_count && ok; j += 2) {
       const int n0 = n_first + j * kBN;
-      const int sb = j & 1;
       if constexpr (kHasDoc) {
 #pragma unroll
         for (int u = 0; u < kBN / 32; ++u) {
           const int kj = n0 + u * 32 + lane;
-          docs_k[sb * kBN + u * 32 + lane] = kj < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
+          docs_k[u * 32 + lane] = kj < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
         }
         __syncwarp();
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, wc, 7));  // warp-uniform
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], (j >> 1) & 1, wc, 7));  // warp-uniform
       if (!ok) break;
       tc_fence_after();
       // whole tile valid?  (below the causal diagonal, inside the window, inside T, no doc ids)
       const bool full = !kHasDoc && (!p.causal || n0 + kBN - 1 <= m0) &&
                         (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (n0 + kBN <= p.T);
-      if (j >= 2) {  // P[sb] is free once O += P_{j-2} V_{j-2} has completed
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[sb], ((j - 2) >> 1) & 1, wc, 8));
+      if (j >= 2) {  // P[wg] is free once O += P_{j-2} V_{j-2} has completed
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[wg], ((j - 2) >> 1) & 1, wc, 8));
         if (!ok) break;
       }
-      // Compact loop (not unrolled over chunks): the pointwise warps must stay inside the
-      // instruction cache; a fully unrolled 128-column body with both mask variants does not.
+      if (full) {
+        // 64 columns per round, both loads in flight before one wait
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_addr + Cfg::kTmemS + sb * kBN + c * 32, r);
-        tmem_wait_ld();
-        uint32_t w[16];
-        if (full) {
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(s_addr + hh * 64, r0);
+          tmem_ld32(s_addr + hh * 64 + 32, r1);
+          tmem_wait_ld();
+          uint32_t w0[16], w1[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float p0 = map.prob(__uint_as_float(r[e]), true);
-            const float p1 = map.prob(__uint_as_float(r[e + 1]), true);
-            w[e / 2] = pack2<true>(p0, p1);
-            zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+            w0[e / 2] = pack2<true>(map.prob(__uint_as_float(r0[e]), true), map.prob(__uint_as_float(r0[e + 1]), true));
+            w1[e / 2] = pack2<true>(map.prob(__uint_as_float(r1[e]), true), map.prob(__uint_as_float(r1[e + 1]), true));
+            zsum += (bf16_lo(w0[e / 2]) + bf16_hi(w0[e / 2])) + (bf16_lo(w1[e / 2]) + bf16_hi(w1[e / 2]));
           }
-        } else {
+          tmem_st16(p_addr + hh * 32, w0);
+          tmem_st16(p_addr + hh * 32 + 16, w1);
+        }
+      } else {
+        // Compact loop (not unrolled over chunks): keeps the masked variant small in the
+        // instruction cache (a fully unrolled 128-column body with both variants does not fit).
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(s_addr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t w[16];
           const int kbase = n0 + c * 32;
-          const int* dk = docs_k + sb * kBN + c * 32;
+          const int* dk = docs_k + c * 32;
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
             float pr[2];
@@ -294,20 +314,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             w[e / 2] = pack2<true>(pr[0], pr[1]);
             zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
           }
+          tmem_st16(p_addr + c * 16, w);
         }
-        tmem_st16(lane_addr + Cfg::kTmemP + sb * (kBN / 2) + c * 16, w);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[sb]);
+      mbar_arrive(&p_full[wg]);
     }
+    // combine the two groups' partial row sums
+    zpart[wg * kBM + row] = zsum;
+    mbar_arrive(z_bar);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(z_bar, 0, wc, 10));
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, wc, 9));
     if (ok) {
       tc_fence_after();
-      const float zden = zsum + p.eps;
+      const float zden = zpart[row] + zpart[kBM + row] + p.eps;
       TO* orow = reinterpret_cast<TO*>(p.out) + (int64_t)b * p.o_s0 + (int64_t)h * p.o_s1 + (int64_t)qi * p.o_s2;
+      // group g stores output columns [g D/2, (g+1) D/2)
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < D / 64; ++cc) {
+        const int c = wg * (D / 64) + cc;
         uint32_t r[32];
         tmem_ld32(lane_addr + Cfg::kTmemO + c * 32, r);
         tmem_wait_ld();
@@ -329,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (qi < p.T) p.z[((int64_t)b * p.H + h) * p.T + qi] = zden;
+      if (qi < p.T && wg == 0) p.z[((int64_t)b * p.H + h) * p.T + qi] = zden;
     }
   }
 

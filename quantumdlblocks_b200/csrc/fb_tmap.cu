@@ -46,4 +46,18 @@ bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, i
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over a row-major fp32 matrix [rows][64] (the dQ accumulator): box (32 floats, 16 rows),
+// 128-byte swizzle.
+bool encode_rows_f32(CUtensorMap* m, float* base, int64_t rows) {
+  if (!get_encoder()) return false;
+  cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {64 * 4};
+  cuuint32_t box[2] = {32, 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace fb
