@@ -1,23 +1,28 @@
 // fb_tc_fwd.cu -- flash-Born forward on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
-// One CTA owns a tile of 128 queries of one (batch, head) and walks the key tiles (128 keys)
-// that can hold valid pairs (causal / window tile skipping, as flash_born.py:152-156).
-// Warp-specialised pipeline (320 threads):
+// Persistent kernel: one CTA per SM walks work items (batch, head, 128-query tile), heaviest
+// first (longest-processing-time order for the causal mask), round-robin over CTAs.  Each item
+// walks the key tiles (128 keys) that can hold valid pairs (causal / window tile skipping, as
+// flash_born.py:152-156).  The tile sequence is flattened across items, so the TMA ring, the
+// TMEM double buffers and the mbarrier phases run on from one item into the next and the
+// per-item set-up latency is hidden.  Warp-specialised pipeline (320 threads):
 //
-//   warp 0      TMA producer: Q tile once, then K_j / V_j through an smem ring of kStages stages
+//   warp 0      TMA producer: Q of an item (double-buffered, the next item's Q is fetched
+//               while the current one runs), K_j and V_j through a ring of kStages stages
+//               with separate K and V barriers (S_j needs only K_j)
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
-//                 S_j = Q K_j^T      tcgen05.mma kind::f16, A = Q (smem, K-major),
-//                                    B = K_j (smem, K-major), D = S[j%2] in TMEM (fp32)
-//                 O  += P_j V_j      A = P[j%2] (TMEM, bf16 packed), B = V_j (smem, MN-major),
-//                                    D = O in TMEM (fp32)
-//               S_{j+1} is issued before O += P_j V_j so the tensor core works while the
-//               pointwise warps turn S_j into P_j.
-//   warps 2-9   two pointwise ("Born") warpgroups; group g handles key tiles j with j % 2 == g
-//               (TMEM buffers S[g], P[g]); thread r of a group owns TMEM lane r = query row r.
-//               tcgen05.ld S row -> a = relu(scale s) (masked), p = a^2, Z += p (fp32),
-//               P = bf16(p) -> tcgen05.st into P[g].  No exp, no running max, no rescale of O:
-//               the epilogue adds the two groups' row sums, reads O once, divides by
-//               Z = sum p + eps and stores O (each group half the columns) and Z.
+//                 S_g = Q K_g^T      tcgen05.mma kind::f16, A = Q (smem, K-major),
+//                                    B = K_g (smem, K-major), D = S[g%2] in TMEM (fp32)
+//                 O  += P_g V_g      A = P[g%2] (TMEM, bf16 packed), B = V_g (smem, MN-major),
+//                                    D = O in TMEM (fp32); the first tile of an item overwrites O
+//               S_{g+1} is issued before O += P_g V_g so the tensor core works while the
+//               pointwise warps turn S_g into P_g.
+//   warps 2-9   two pointwise ("Born") warpgroups; group w handles the tiles with g % 2 == w
+//               (TMEM buffers S[w], P[w]); thread r of a group owns TMEM lane r = query row r.
+//               tcgen05.ld S row -> a = relu(scale s) (masked), p = a^2, P = bf16(p) ->
+//               tcgen05.st into P[w], Z += the bf16-rounded p.  No exp, no running max, no
+//               rescale of O: per item the groups add their row sums, read O once, multiply by
+//               1 / Z (Z = sum p + eps) and store O (each group half the columns) and Z.
 //
 // Numerics: S and O accumulate in fp32 and PV consumes p rounded to bf16, as in the reference
 // kernel (flash_born.py:156-191).  Z sums the same bf16-rounded p that PV consumes (the reference
@@ -25,8 +30,11 @@
 // valid key returns that key's v exactly, and the backward's delta = dO.O cancels against dO.v
 // without the bf16 rounding of p (which the 2/a factor of dS would otherwise amplify).
 //
-// TMEM columns (512 allocated): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D).
+// TMEM columns (512): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D);
+// for d=64 also Z [448,464): the row sums, produced by the tensor core as P times a ones tile.
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "fb_common.cuh"
 #include "fb_sm100.cuh"
@@ -36,29 +44,34 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128;      // queries per CTA (one M=128 MMA)
-constexpr int kBN = 128;      // keys per tile
-constexpr int kThreads = 320; // 10 warps
+constexpr int kBM = 128;       // queries per item (one M=128 MMA)
+constexpr int kBN = 128;       // keys per tile
+constexpr int kThreads = 320;  // 10 warps
 constexpr uint32_t kTmemCols = 512;
 
 template <int D>
 struct FwdCfg {
-  static constexpr int kStages = D == 64 ? 3 : 2;
+  static constexpr int kStages = D == 64 ? 5 : 2;
+  // d=64: Z comes from the tensor core (P times a ones tile into 16 spare TMEM columns); d=128
+  // has no spare columns and sums Z in the pointwise warps
+  static constexpr bool kTcZ = D == 64;
   static constexpr int kHalves = D / 64;                // 64-column halves of a head
   static constexpr uint32_t kTileBytes = kBN * D * 2;   // one K or V tile (== one Q tile)
   static constexpr uint32_t kHalfBytes = kBN * 64 * 2;  // 16 KB
-  static constexpr uint32_t kQOff = 0;
-  static constexpr uint32_t kKOff = kTileBytes;
+  static constexpr uint32_t kQOff = 0;                  // Q[2]
+  static constexpr uint32_t kKOff = 2 * kTileBytes;
   static constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
-  static constexpr uint32_t kBarOff = kVOff + kStages * kTileBytes;
-  static constexpr uint32_t kDocOff = kBarOff + 256;             // [8 warps][kBN] int32
-  static constexpr uint32_t kZOff = kDocOff + 8 * kBN * 4;         // [2 groups][kBM] fp32 row sums
-  static constexpr uint32_t kSmemBytes = kZOff + 2 * kBM * 4;
-  static constexpr uint32_t kTmemS = 0, kTmemP = 256, kTmemO = 384;
+  static constexpr uint32_t kOnesOff = kVOff + kStages * kTileBytes;  // 16 rows x 128 B of bf16 ones
+  static constexpr uint32_t kBarOff = kOnesOff + 2048;
+  static constexpr uint32_t kDocOff = kBarOff + 512;             // [8 warps][kBN] int32
+  static constexpr uint32_t kZOff = kDocOff + 8 * kBN * 4;         // [2 items][2 groups][kBM] fp32
+  static constexpr uint32_t kSmemBytes = kZOff + 4 * kBM * 4;
+  static constexpr uint32_t kTmemS = 0, kTmemP = 256, kTmemO = 384, kTmemZ = 448;
 };
 
 struct FwdParams {
   int B, H, T;
+  int n_mt, n_items;  // query tiles per head, work items
   int causal, window;
   float eps, eps_base;
   const float* scale;
@@ -83,14 +96,26 @@ template <> struct TcMap<PurifiedMap> {
   }
 };
 
-// Key-tile range [first, first + count) of query tile m0 (tiles of kBN keys, aligned to kBN).
-__device__ __forceinline__ void key_tiles(const FwdParams& p, int m0, int& n_first, int& n_count) {
+struct Item {
+  int b, h, m0, n_first, n_count;
+};
+
+// Work item idx: latest query tiles (the most keys under a causal mask) first, then (b, h).
+__device__ __forceinline__ Item item_at(const FwdParams& p, int idx) {
+  const int bh_total = p.B * p.H;
+  const int mt = p.n_mt - 1 - idx / bh_total;
+  const int bh = idx % bh_total;
+  Item it;
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  it.m0 = mt * kBM;
   int lo = 0, hi = p.T;
-  if (p.causal) hi = min(p.T, m0 + kBM);
-  if (p.window > 0) lo = max(0, m0 - p.window + 1);
+  if (p.causal) hi = min(p.T, it.m0 + kBM);
+  if (p.window > 0) lo = max(0, it.m0 - p.window + 1);
   lo = (lo / kBN) * kBN;
-  n_first = lo;
-  n_count = hi > lo ? (hi - lo + kBN - 1) / kBN : 0;
+  it.n_first = lo;
+  it.n_count = hi > lo ? (hi - lo + kBN - 1) / kBN : 0;
+  return it;
 }
 
 template <int D, class Map, bool kHasDoc, typename TO>
@@ -100,48 +125,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Cfg = FwdCfg<D>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-byte swizzle atoms
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOff);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;             // [S]
-  uint64_t* kv_empty = bars + 1 + S;        // [S]
-  uint64_t* s_full = bars + 1 + 2 * S;      // [2]
-  uint64_t* p_full = bars + 3 + 2 * S;      // [2]
-  uint64_t* pv_done = bars + 5 + 2 * S;     // [2]
-  uint64_t* o_full = bars + 7 + 2 * S;
-  uint64_t* drain = bars + 8 + 2 * S;
-  uint64_t* z_bar = bars + 9 + 2 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 17);
-  int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);  // per pointwise warp: [kBN]
+  uint64_t* q_full = bars + 0;           // [2]
+  uint64_t* q_empty = bars + 2;          // [2]
+  uint64_t* k_full = bars + 4;           // [S]
+  uint64_t* v_full = bars + 4 + S;       // [S]
+  uint64_t* kv_empty = bars + 4 + 2 * S; // [S]
+  uint64_t* s_full = bars + 4 + 3 * S;   // [2]
+  uint64_t* p_full = bars + 6 + 3 * S;   // [2]
+  uint64_t* pv_done = bars + 8 + 3 * S;  // [2]
+  uint64_t* o_full = bars + 10 + 3 * S;
+  uint64_t* o_empty = bars + 11 + 3 * S;
+  uint64_t* z_bar = bars + 12 + 3 * S;
+  uint64_t* drain = bars + 13 + 3 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 33);
+  int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);
   float* zpart = reinterpret_cast<float*>(smem + Cfg::kZOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = gridDim.x - 1 - blockIdx.x;  // latest (heaviest causal) query tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int m0 = tile * kBM;
-  int n_first, n_count;
-  key_tiles(p, m0, n_first, n_count);
   const WaitCtx wc{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_done[i], 1);
     }
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&k_full[st], 1);
+      mbar_init(&v_full[st], 1);
+      mbar_init(&kv_empty[st], 1);
+    }
     mbar_init(o_full, 1);
-    mbar_init(drain, 1);
+    mbar_init(o_empty, 256);
     mbar_init(z_bar, 256);
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if constexpr (Cfg::kTcZ) {  // the ones tile read by the Z product (B operand)
+    uint32_t* ones = reinterpret_cast<uint32_t*>(smem + Cfg::kOnesOff);
+    for (int x = threadIdx.x; x < 2048 / 4; x += kThreads) ones[x] = 0x3F803F80u;  // bf16 1.0 pairs
+    fence_proxy_async_smem();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tmQ);
@@ -160,30 +190,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
-      int issued = 0;
       bool ok = true;
-      mbar_arrive_expect_tx(q_full, Cfg::kTileBytes);
+      int g = 0, i = 0, q_issued = 0;
+      auto load_q = [&](int item_seq, const Item& it) -> bool {
+        const int qb = item_seq & 1;
+        if (item_seq >= 2 && !mbar_wait(&q_empty[qb], ((item_seq >> 1) - 1) & 1, wc, 1)) return false;
+        mbar_arrive_expect_tx(&q_full[qb], Cfg::kTileBytes);
 #pragma unroll
-      for (int hf = 0; hf < Cfg::kHalves; ++hf)
-        tma_load_4d(smem + Cfg::kQOff + hf * Cfg::kHalfBytes, &tmQ, q_full, hf * 64, m0, h, b);
-      for (int j = 0; j < n_count && ok; ++j) {
-        const int st = j % S;
-        if (j >= S) ok = mbar_wait(&kv_empty[st], ((j / S) - 1) & 1, wc, 1);
-        if (!ok) break;
-        const int n0 = n_first + j * kBN;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * Cfg::kTileBytes);
+        for (int hf = 0; hf < Cfg::kHalves; ++hf)
+          tma_load_4d(smem + Cfg::kQOff + qb * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmQ, &q_full[qb], hf * 64,
+                      it.m0, it.h, it.b);
+        q_issued = item_seq + 1;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+        const Item it = item_at(p, idx);
+        if (q_issued <= i) ok = load_q(i, it);
+        for (int t = 0; t < it.n_count && ok; ++t, ++g) {
+          const int st = g % S;
+          if (g >= S) ok = mbar_wait(&kv_empty[st], ((g / S) - 1) & 1, wc, 2);
+          if (!ok) break;
+          const int n0 = it.n_first + t * kBN;
+          mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
 #pragma unroll
-        for (int hf = 0; hf < Cfg::kHalves; ++hf) {
-          tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmK, &kv_full[st], hf * 64,
-                      n0, h, b);
-          tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmV, &kv_full[st], hf * 64,
-                      n0, h, b);
+          for (int hf = 0; hf < Cfg::kHalves; ++hf)
+            tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmK, &k_full[st], hf * 64,
+                        n0, it.h, it.b);
+          mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
+#pragma unroll
+          for (int hf = 0; hf < Cfg::kHalves; ++hf)
+            tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmV, &v_full[st], hf * 64,
+                        n0, it.h, it.b);
+          // once the first K/V of this item is on its way, fetch the next item's Q
+          if (t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_q(i + 1, item_at(p, idx + gridDim.x));
         }
-        issued = j + 1;
       }
       if (!ok) {
         // abandoned: let the copies already in flight land before the CTA exits
-        for (int j = max(0, issued - S); j < issued; ++j) mbar_wait_drain(&kv_full[j % S], (j / S) & 1);
+        for (int gg = max(0, g - S); gg < g; ++gg) {
+          mbar_wait_drain(&k_full[gg % S], (gg / S) & 1);
+          mbar_wait_drain(&v_full[gg % S], (gg / S) & 1);
+        }
+        for (int qq = max(0, q_issued - 2); qq < q_issued; ++qq) mbar_wait_drain(&q_full[qq & 1], (qq >> 1) & 1);
       }
     }
     __syncwarp();
@@ -192,44 +240,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       constexpr uint32_t idS = idesc_f16(1, 0, 0, kBN, kBM);  // S: A K-major, B K-major, N = 128
       constexpr uint32_t idO = idesc_f16(1, 0, 1, D, kBM);    // O: A TMEM, B MN-major, N = D
-      const uint32_t q_base = smem_u32(smem + Cfg::kQOff);
-      bool ok = mbar_wait(q_full, 0, wc, 3);
-      for (int j = 0; j <= n_count && ok; ++j) {
-        if (j < n_count) {
-          const int st = j % S;
-          ok = mbar_wait(&kv_full[st], (j / S) & 1, wc, 4);
+      constexpr uint32_t idZ = idesc_f16(1, 0, 1, 16, kBM);   // Z: A TMEM (P), B = ones, N = 16
+      const uint32_t ones_base = smem_u32(smem + Cfg::kOnesOff);
+      bool ok = true;
+      int g = 0, i = 0;
+      // pending O += P V of the previous tile
+      bool have_prev = false;
+      int pv_g = 0, pv_i = 0, pv_st = 0;
+      bool pv_first = false, pv_last = false;
+      auto issue_pv = [&]() -> bool {
+        if (!mbar_wait(&p_full[pv_g & 1], (pv_g >> 1) & 1, wc, 5)) return false;
+        if (!mbar_wait(&v_full[pv_st], (pv_g / S) & 1, wc, 6)) return false;
+        if (pv_first && pv_i >= 1 && !mbar_wait(o_empty, (pv_i - 1) & 1, wc, 7)) return false;
+        tc_fence_after();
+        const uint32_t v_base = smem_u32(smem + Cfg::kVOff + pv_st * Cfg::kTileBytes);
+        const uint32_t a_p = tmem + Cfg::kTmemP + (pv_g & 1) * (kBN / 2);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile
+          mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(v_base + kk * 2048, Cfg::kHalfBytes, 1024), idO,
+                 (pv_first && kk == 0) ? 0u : 1u);
+        }
+        if constexpr (Cfg::kTcZ) {
+          // Z += P 1: every B row is ones, so each K step reads the same 16-row ones tile
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            mma_ts(tmem + Cfg::kTmemZ, a_p + kk * 8, sdesc_sw128(ones_base, 1024, 1024), idZ,
+                   (pv_first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&kv_empty[pv_st]);
+        mma_commit(&pv_done[pv_g & 1]);
+        if (pv_last) mma_commit(o_full);
+        have_prev = false;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+        const Item it = item_at(p, idx);
+        if (have_prev) ok = issue_pv();  // finish the previous item before waiting on this one
+        if (ok) ok = mbar_wait(&q_full[i & 1], (i >> 1) & 1, wc, 3);
+        const uint32_t q_base = smem_u32(smem + Cfg::kQOff + (i & 1) * Cfg::kTileBytes);
+        for (int t = 0; t < it.n_count && ok; ++t, ++g) {
+          const int st = g % S;
+          ok = mbar_wait(&k_full[st], (g / S) & 1, wc, 4);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(smem + Cfg::kKOff + st * Cfg::kTileBytes);
-          const uint32_t d_s = tmem + Cfg::kTmemS + (j & 1) * kBN;
+          const uint32_t d_s = tmem + Cfg::kTmemS + (g & 1) * kBN;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint32_t off = (kk >> 2) * Cfg::kHalfBytes + (kk & 3) * 32;
             mma_ss(d_s, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024), idS, kk > 0);
           }
-          mma_commit(&s_full[j & 1]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int st = jj % S;
-          ok = mbar_wait(&p_full[jj & 1], (jj >> 1) & 1, wc, 5);
+          mma_commit(&s_full[g & 1]);
+          if (t == it.n_count - 1) mma_commit(&q_empty[i & 1]);
+          if (have_prev) ok = issue_pv();
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t v_base = smem_u32(smem + Cfg::kVOff + st * Cfg::kTileBytes);
-          const uint32_t a_p = tmem + Cfg::kTmemP + (jj & 1) * (kBN / 2);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile
-            mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(v_base + kk * 2048, Cfg::kHalfBytes, 1024), idO,
-                   (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(&kv_empty[st]);
-          mma_commit(&pv_done[jj & 1]);
+          have_prev = true;
+          pv_g = g;
+          pv_i = i;
+          pv_st = st;
+          pv_first = t == 0;
+          pv_last = t == it.n_count - 1;
         }
       }
-      if (ok) {
-        mma_commit(o_full);
-      } else {
+      if (ok && have_prev) ok = issue_pv();
+      if (!ok) {
         mma_commit(drain);  // wait for every MMA in flight before TMEM is released
         mbar_wait_drain(drain, 0);
       }
@@ -237,125 +312,162 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ pointwise warpgroups
-    // Warpgroup g (warps 2+4g .. 5+4g) turns the S tiles j with j % 2 == g into P, so it always
-    // uses TMEM buffer S[g]/P[g]; the two groups' TMEM latency chains interleave on the SM.
     const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;              // TMEM lane group of this warp
     const int row = lg * 32 + lane;       // query row within the tile == TMEM lane
-    const int qi = m0 + row;
     int* docs_k = docs_all + (wg * 4 + lg) * kBN;  // this warp's copy of the key tile's doc ids
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
     const uint32_t s_addr = lane_addr + Cfg::kTmemS + wg * kBN;
     const uint32_t p_addr = lane_addr + Cfg::kTmemP + wg * (kBN / 2);
-    const Map map = TcMap<Map>::make(p, h);
-    int doc_i = 0;
-    if constexpr (kHasDoc) doc_i = qi < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
-    float zsum = 0.f;
     bool ok = true;
-    for (int j = wg; j < n_count && ok; j += 2) {
-      const int n0 = n_first + j * kBN;
-      if constexpr (kHasDoc) {
+    int g = 0, i = 0;
+    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      const Item it = item_at(p, idx);
+      const int qi = it.m0 + row;
+      const Map map = TcMap<Map>::make(p, it.h);
+      int doc_i = 0;
+      if constexpr (kHasDoc) doc_i = qi < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+      float zsum = 0.f;
+      for (int t = (wg - g) & 1; t < it.n_count && ok; t += 2) {
+        const int gg = g + t;  // gg % 2 == wg
+        const int n0 = it.n_first + t * kBN;
+        if constexpr (kHasDoc) {
 #pragma unroll
-        for (int u = 0; u < kBN / 32; ++u) {
-          const int kj = n0 + u * 32 + lane;
-          docs_k[u * 32 + lane] = kj < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
+          for (int u = 0; u < kBN / 32; ++u) {
+            const int kj = n0 + u * 32 + lane;
+            docs_k[u * 32 + lane] = kj < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
+          }
+          __syncwarp();
         }
-        __syncwarp();
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], (gg >> 1) & 1, wc, 8));  // warp-uniform
+        if (!ok) break;
+        tc_fence_after();
+        // whole tile valid?  (below the causal diagonal, inside the window, inside T, no doc ids)
+        const bool full = !kHasDoc && (!p.causal || n0 + kBN - 1 <= it.m0) &&
+                          (p.window <= 0 || (it.m0 + kBM - 1) - n0 < p.window) && (n0 + kBN <= p.T);
+        if (gg >= 2) {  // P[wg] is free once O += P_{gg-2} V_{gg-2} has completed
+          ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[wg], ((gg - 2) >> 1) & 1, wc, 9));
+          if (!ok) break;
+        }
+        // causal diagonal tile (the item's own 128 keys): chunk c of warp lg is entirely valid for
+        // c < lg, entirely masked for c > lg, and valid for column e <= lane when c == lg
+        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 == it.m0;
+        if (full) {
+          // 64 columns per round, both loads in flight before one wait
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(s_addr + hh * 64, r0);
+            tmem_ld32(s_addr + hh * 64 + 32, r1);
+            tmem_wait_ld();
+            uint32_t w0[16], w1[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              w0[e / 2] = pack2<true>(map.prob(__uint_as_float(r0[e]), true), map.prob(__uint_as_float(r0[e + 1]), true));
+              w1[e / 2] = pack2<true>(map.prob(__uint_as_float(r1[e]), true), map.prob(__uint_as_float(r1[e + 1]), true));
+              if constexpr (!Cfg::kTcZ)
+                zsum += (bf16_lo(w0[e / 2]) + bf16_hi(w0[e / 2])) + (bf16_lo(w1[e / 2]) + bf16_hi(w1[e / 2]));
+            }
+            tmem_st16(p_addr + hh * 32, w0);
+            tmem_st16(p_addr + hh * 32 + 16, w1);
+          }
+        } else if (diag) {
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t w[16];
+            if (c > lg) {  // keys above the diagonal for every row of this warp
+#pragma unroll
+              for (int e = 0; e < 16; ++e) w[e] = 0u;
+            } else {
+              uint32_t r[32];
+              tmem_ld32(s_addr + c * 32, r);
+              tmem_wait_ld();
+              const int lim = c < lg ? 31 : lane;
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), e <= lim),
+                                       map.prob(__uint_as_float(r[e + 1]), e + 1 <= lim));
+                if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+              }
+            }
+            tmem_st16(p_addr + c * 16, w);
+          }
+        } else {
+          // Compact loop (not unrolled over chunks): keeps the masked variant small in the
+          // instruction cache (a fully unrolled 128-column body with both variants does not fit).
+#pragma unroll 1
+          for (int c = 0; c < kBN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(s_addr + c * 32, r);
+            tmem_wait_ld();
+            uint32_t w[16];
+            const int kbase = n0 + c * 32;
+            const int* dk = docs_k + c * 32;
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float pr[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                int doc_j = 0;
+                if constexpr (kHasDoc) doc_j = dk[e + u];
+                const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
+                pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
+              }
+              w[e / 2] = pack2<true>(pr[0], pr[1]);
+              if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+            }
+            tmem_st16(p_addr + c * 16, w);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[wg]);
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], (j >> 1) & 1, wc, 7));  // warp-uniform
+      // ---- epilogue of the item: Z (tensor-core sum, or the two groups' row sums), O * (1 / Z)
+      float* zp = zpart + (i & 1) * 2 * kBM;
+      if constexpr (!Cfg::kTcZ) {
+        zp[wg * kBM + row] = zsum;
+        mbar_arrive(z_bar);
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(z_bar, i & 1, wc, 10));
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, i & 1, wc, 11));
       if (!ok) break;
       tc_fence_after();
-      // whole tile valid?  (below the causal diagonal, inside the window, inside T, no doc ids)
-      const bool full = !kHasDoc && (!p.causal || n0 + kBN - 1 <= m0) &&
-                        (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (n0 + kBN <= p.T);
-      if (j >= 2) {  // P[wg] is free once O += P_{j-2} V_{j-2} has completed
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[wg], ((j - 2) >> 1) & 1, wc, 8));
-        if (!ok) break;
-      }
-      if (full) {
-        // 64 columns per round, both loads in flight before one wait
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(s_addr + hh * 64, r0);
-          tmem_ld32(s_addr + hh * 64 + 32, r1);
-          tmem_wait_ld();
-          uint32_t w0[16], w1[16];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            w0[e / 2] = pack2<true>(map.prob(__uint_as_float(r0[e]), true), map.prob(__uint_as_float(r0[e + 1]), true));
-            w1[e / 2] = pack2<true>(map.prob(__uint_as_float(r1[e]), true), map.prob(__uint_as_float(r1[e + 1]), true));
-            zsum += (bf16_lo(w0[e / 2]) + bf16_hi(w0[e / 2])) + (bf16_lo(w1[e / 2]) + bf16_hi(w1[e / 2]));
-          }
-          tmem_st16(p_addr + hh * 32, w0);
-          tmem_st16(p_addr + hh * 32 + 16, w1);
-        }
+      float zden;
+      if constexpr (Cfg::kTcZ) {
+        zden = __uint_as_float(tmem_ld1(lane_addr + Cfg::kTmemZ)) + p.eps;
       } else {
-        // Compact loop (not unrolled over chunks): keeps the masked variant small in the
-        // instruction cache (a fully unrolled 128-column body with both variants does not fit).
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(s_addr + c * 32, r);
-          tmem_wait_ld();
-          uint32_t w[16];
-          const int kbase = n0 + c * 32;
-          const int* dk = docs_k + c * 32;
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            float pr[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              int doc_j = 0;
-              if constexpr (kHasDoc) doc_j = dk[e + u];
-              const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
-              pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
-            }
-            w[e / 2] = pack2<true>(pr[0], pr[1]);
-            zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
-          }
-          tmem_st16(p_addr + c * 16, w);
-        }
+        zden = zp[row] + zp[kBM + row] + p.eps;
       }
-      tmem_wait_st();
+      const float inv = 1.f / zden;
+      uint32_t r[D / 2];
+      // group wg handles output columns [wg D/2, (wg+1) D/2)
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc) tmem_ld32(lane_addr + Cfg::kTmemO + wg * (D / 2) + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(r + cc * 32));
+      tmem_wait_ld();
       tc_fence_before();
-      mbar_arrive(&p_full[wg]);
-    }
-    // combine the two groups' partial row sums
-    zpart[wg * kBM + row] = zsum;
-    mbar_arrive(z_bar);
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(z_bar, 0, wc, 10));
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, wc, 9));
-    if (ok) {
-      tc_fence_after();
-      const float zden = zpart[row] + zpart[kBM + row] + p.eps;
-      TO* orow = reinterpret_cast<TO*>(p.out) + (int64_t)b * p.o_s0 + (int64_t)h * p.o_s1 + (int64_t)qi * p.o_s2;
-      // group g stores output columns [g D/2, (g+1) D/2)
+      mbar_arrive(o_empty);
+      if (qi < p.T) {
+        TO* orow = reinterpret_cast<TO*>(p.out) + (int64_t)it.b * p.o_s0 + (int64_t)it.h * p.o_s1 +
+                   (int64_t)qi * p.o_s2 + wg * (D / 2);
+        if constexpr (sizeof(TO) == 2) {
+          uint4* dst = reinterpret_cast<uint4*>(orow);
 #pragma unroll
-      for (int cc = 0; cc < D / 64; ++cc) {
-        const int c = wg * (D / 64) + cc;
-        uint32_t r[32];
-        tmem_ld32(lane_addr + Cfg::kTmemO + c * 32, r);
-        tmem_wait_ld();
-        if (qi < p.T) {
-          if constexpr (sizeof(TO) == 2) {
-            uint32_t w[16];
+          for (int v4 = 0; v4 < D / 16; ++v4)
+            dst[v4] = make_uint4(pack2<true>(__uint_as_float(r[8 * v4]) * inv, __uint_as_float(r[8 * v4 + 1]) * inv),
+                                 pack2<true>(__uint_as_float(r[8 * v4 + 2]) * inv, __uint_as_float(r[8 * v4 + 3]) * inv),
+                                 pack2<true>(__uint_as_float(r[8 * v4 + 4]) * inv, __uint_as_float(r[8 * v4 + 5]) * inv),
+                                 pack2<true>(__uint_as_float(r[8 * v4 + 6]) * inv, __uint_as_float(r[8 * v4 + 7]) * inv));
+        } else {
+          float4* dst = reinterpret_cast<float4*>(orow);
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w[e] = pack2<true>(__uint_as_float(r[2 * e]) / zden, __uint_as_float(r[2 * e + 1]) / zden);
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) dst[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
-          } else {
-            float4* dst = reinterpret_cast<float4*>(orow + c * 32);
-#pragma unroll
-            for (int v4 = 0; v4 < 8; ++v4)
-              dst[v4] = make_float4(__uint_as_float(r[4 * v4]) / zden, __uint_as_float(r[4 * v4 + 1]) / zden,
-                                    __uint_as_float(r[4 * v4 + 2]) / zden, __uint_as_float(r[4 * v4 + 3]) / zden);
-          }
+          for (int v4 = 0; v4 < D / 8; ++v4)
+            dst[v4] = make_float4(__uint_as_float(r[4 * v4]) * inv, __uint_as_float(r[4 * v4 + 1]) * inv,
+                                  __uint_as_float(r[4 * v4 + 2]) * inv, __uint_as_float(r[4 * v4 + 3]) * inv);
         }
+        if (wg == 0) p.z[((int64_t)it.b * p.H + it.h) * p.T + qi] = zden;
       }
-      if (qi < p.T && wg == 0) p.z[((int64_t)b * p.H + h) * p.T + qi] = zden;
+      g += it.n_count;
     }
   }
 
@@ -370,6 +482,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n = v;
+    else
+      n = 148;
+  }
+  return n;
+}
+
 template <int D, class Map, bool kHasDoc, typename TO>
 int launch_fwd(const Problem& pr, cudaStream_t s, const FwdParams& fp, const CUtensorMap& mq, const CUtensorMap& mk,
                const CUtensorMap& mv) {
@@ -377,7 +501,7 @@ int launch_fwd(const Problem& pr, cudaStream_t s, const FwdParams& fp, const CUt
   const uint32_t smem = FwdCfg<D>::kSmemBytes + 1024;  // + alignment slack
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
-  dim3 grid((pr.T + kBM - 1) / kBM, pr.H, pr.B);
+  dim3 grid(std::min(fp.n_items, num_sms()));
   kernel<<<grid, kThreads, smem, s>>>(mq, mk, mv, fp);
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
@@ -417,6 +541,8 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
     return FB_ERR_ALIGN;
   FwdParams fp{};
   fp.B = pr.B; fp.H = pr.H; fp.T = pr.T;
+  fp.n_mt = (pr.T + kBM - 1) / kBM;
+  fp.n_items = fp.n_mt * pr.B * pr.H;
   fp.causal = pr.causal; fp.window = pr.window;
   fp.eps = pr.eps; fp.eps_base = pr.eps_base;
   fp.scale = pr.scale; fp.scale_per_head = pr.scale_per_head;
