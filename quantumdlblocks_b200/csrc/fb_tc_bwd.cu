@@ -3,9 +3,11 @@
 // Three launches (all on the caller's stream):
 //   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
 //                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
-//   2. tc_bwd_kernel     one CTA per (batch, head, 128-key tile); walks the 64-query tiles that
-//                        can hold valid pairs and accumulates dK, dV in TMEM; dQ partials are
-//                        reduced into the fp32 accumulator with TMA tensor reduce-add
+//   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile),
+//                        heaviest first; each item walks the 64-query tiles that can hold valid
+//                        pairs and accumulates dK, dV in TMEM; dQ partials are reduced into the
+//                        fp32 accumulator with TMA tensor reduce-add.  The query-tile pipeline
+//                        runs on across items (K, V double-buffered per item)
 //   3. bwd_post_kernel   dQ = accumulator -> input dtype
 //   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
 //                        sums and the main kernel's per-CTA partials
@@ -30,6 +32,8 @@
 // TMEM columns: S^T[0..1] 0/64, dP^T[0..1] 128/192, dV 256, dK 320, dQ[0..1] 384/448.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "fb_common.cuh"
 #include "fb_sm100.cuh"
 
@@ -46,13 +50,13 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTS = 0, kTdP = 128, kTdV = 256, kTdK = 320, kTdQ = 384;
 
 // shared memory carve-up (bytes from the 1024-aligned base)
-constexpr uint32_t kSK = 0;                    // K tile 128 x 64 bf16     16 KB
-constexpr uint32_t kSV = 16384;                // V tile                    16 KB
-constexpr uint32_t kSQ = 32768;                // Q stages [2] 64 x 64       8 KB each
-constexpr uint32_t kSdO = 49152;               // dO stages [2]              8 KB each
-constexpr uint32_t kSG = 65536;                // G [2] 128 keys x 64 q      16 KB each
-constexpr uint32_t kSStg = 98304;              // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
-constexpr uint32_t kSVec = 131072;             // dlz[2][64] (delta / Z), zinv[2][64] (1 / Z) fp32
+constexpr uint32_t kSK = 0;                    // K tiles [2 items] 128 x 64 bf16, 32 KB apart (K, V interleaved)
+constexpr uint32_t kSV = 16384;                // V tiles [2 items]
+constexpr uint32_t kSQ = 65536;                // Q stages [2] 64 x 64       8 KB each
+constexpr uint32_t kSdO = 81920;               // dO stages [2]              8 KB each
+constexpr uint32_t kSG = 98304;                // G [2] 128 keys x 64 q      16 KB each
+constexpr uint32_t kSStg = 131072;             // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
+constexpr uint32_t kSVec = 163840;             // dlz[2][64] (delta / Z), zinv[2][64] (1 / Z) fp32
 constexpr uint32_t kSDoc = kSVec + 1024;       // query doc ids [8 warps][64] int32
 constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
 constexpr uint32_t kSmemBytes = kSBar + 256;
@@ -74,8 +78,8 @@ struct BwdParams {
   const float* dlz;    // [BH][Tpad]  delta_i / Z_i
   const float* zinv;   // [BH][Tpad]  1 / Z_i
   float* dq_acc;       // [BH][Tpad][64]
-  float* partials;     // [BH][n_kv][2]
-  int n_kv;
+  float* partials;     // [BH][n_kv][8 warps][2]
+  int n_kv, n_items;
   int* status;
 };
 
@@ -97,14 +101,27 @@ template <> struct BwdMap<PurifiedMapTC> {
   }
 };
 
-// Query tiles [m_first, m_first + 64 * count) that can hold valid pairs for keys [n0, n0 + kBN).
-__device__ __forceinline__ void query_tiles(const BwdParams& p, int n0, int& m_first, int& count) {
-  int lo = p.causal ? n0 : 0;
+struct BwdItem {
+  int b, h, kt, n0, m_first, n_tiles;
+};
+
+// Work item idx: early key tiles (the most queries under a causal mask) first, then (b, h).
+// Query tiles [m_first, m_first + 64 n_tiles) can hold valid pairs for keys [n0, n0 + kBN).
+__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int idx) {
+  const int bh_total = p.B * p.H;
+  BwdItem it;
+  it.kt = idx / bh_total;
+  const int bh = idx % bh_total;
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  it.n0 = it.kt * kBN;
+  int lo = p.causal ? it.n0 : 0;
   int hi = p.T;
-  if (p.window > 0) hi = min(p.T, n0 + kBN - 1 + p.window);
+  if (p.window > 0) hi = min(p.T, it.n0 + kBN - 1 + p.window);
   lo = (lo / kBM) * kBM;
-  m_first = lo;
-  count = hi > lo ? (hi - lo + kBM - 1) / kBM : 0;
+  it.m_first = lo;
+  it.n_tiles = hi > lo ? (hi - lo + kBM - 1) / kBM : 0;
+  return it;
 }
 
 template <class Map, bool kHasDoc>
@@ -115,35 +132,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;     // [2]
-  uint64_t* q_empty = bars + 3;    // [2]
-  uint64_t* sdp_full = bars + 5;   // [2]
-  uint64_t* wg_full = bars + 7;    // [2]
-  uint64_t* mma_done = bars + 9;   // [2]
-  uint64_t* dq_full = bars + 11;   // [2]
-  uint64_t* dq_empty = bars + 13;  // [2]
-  uint64_t* acc_full = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18);
-  float* red = reinterpret_cast<float*>(bars + 19);  // [8 pointwise warps][2]
+  uint64_t* kv_full = bars + 0;    // [2] per item parity
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* q_full = bars + 4;     // [2] per query-tile parity
+  uint64_t* q_empty = bars + 6;    // [2]
+  uint64_t* sdp_full = bars + 8;   // [2]
+  uint64_t* wg_full = bars + 10;   // [2]
+  uint64_t* mma_done = bars + 12;  // [2]
+  uint64_t* dq_full = bars + 14;   // [2]
+  uint64_t* dq_empty = bars + 16;  // [2]
+  uint64_t* acc_full = bars + 18;
+  uint64_t* acc_empty = bars + 19;
+  uint64_t* drain = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 22);
   float* vdlz = reinterpret_cast<float*>(smem + kSVec);          // [2][64]
   float* vzinv = reinterpret_cast<float*>(smem + kSVec + 512);   // [2][64]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int ktile = blockIdx.x;  // early key tiles see the most queries under a causal mask
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int n0 = ktile * kBN;
-  const int64_t bh = (int64_t)b * p.H + h;
-  int m_first, n_tiles;
-  query_tiles(p, n0, m_first, n_tiles);
   const WaitCtx wc{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&sdp_full[i], 1);
@@ -153,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&dq_empty[i], 128);
     }
     mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -177,25 +191,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       bool ok = true;
-      int issued = 0;
-      mbar_arrive_expect_tx(kv_full, 2 * kBN * kD * 2);
-      tma_load_4d(smem + kSK, &tmK, kv_full, 0, n0, h, b);
-      tma_load_4d(smem + kSV, &tmV, kv_full, 0, n0, h, b);
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        const int st = t & 1;
-        if (t >= 2) ok = mbar_wait(&q_empty[st], ((t >> 1) - 1) & 1, wc, 21);
-        if (!ok) break;
-        const int m0 = m_first + t * kBM;
-        mbar_arrive_expect_tx(&q_full[st], 2 * kBM * kD * 2 + 2 * kBM * 4);
-        tma_load_4d(smem + kSQ + st * 8192, &tmQ, &q_full[st], 0, m0, h, b);
-        tma_load_4d(smem + kSdO + st * 8192, &tmdO, &q_full[st], 0, m0, h, b);
-        bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
-        bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
-        issued = t + 1;
+      int g = 0, i = 0, kv_issued = 0;
+      auto load_kv = [&](int item_seq, const BwdItem& it) -> bool {
+        const int kb = item_seq & 1;
+        if (item_seq >= 2 && !mbar_wait(&kv_empty[kb], ((item_seq >> 1) - 1) & 1, wc, 20)) return false;
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * kBN * kD * 2);
+        tma_load_4d(smem + kSK + kb * 32768, &tmK, &kv_full[kb], 0, it.n0, it.h, it.b);
+        tma_load_4d(smem + kSV + kb * 32768, &tmV, &kv_full[kb], 0, it.n0, it.h, it.b);
+        kv_issued = item_seq + 1;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+        const BwdItem it = bwd_item(p, idx);
+        const int64_t bh = (int64_t)it.b * p.H + it.h;
+        if (kv_issued <= i) ok = load_kv(i, it);
+        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
+          const int st = g & 1;
+          if (g >= 2) ok = mbar_wait(&q_empty[st], ((g >> 1) - 1) & 1, wc, 21);
+          if (!ok) break;
+          const int m0 = it.m_first + t * kBM;
+          mbar_arrive_expect_tx(&q_full[st], 2 * kBM * kD * 2 + 2 * kBM * 4);
+          tma_load_4d(smem + kSQ + st * 8192, &tmQ, &q_full[st], 0, m0, it.h, it.b);
+          tma_load_4d(smem + kSdO + st * 8192, &tmdO, &q_full[st], 0, m0, it.h, it.b);
+          bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
+          bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
+          // once this item's first query tile is on its way, fetch the next item's K and V
+          if (t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_kv(i + 1, bwd_item(p, idx + gridDim.x));
+        }
       }
       if (!ok) {
-        mbar_wait_drain(kv_full, 0);
-        for (int t = max(0, issued - 2); t < issued; ++t) mbar_wait_drain(&q_full[t & 1], (t >> 1) & 1);
+        for (int gg = max(0, g - 2); gg < g; ++gg) mbar_wait_drain(&q_full[gg & 1], (gg >> 1) & 1);
+        for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_wait_drain(&kv_full[ii & 1], (ii >> 1) & 1);
       }
     }
     __syncwarp();
@@ -205,13 +231,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idSdP = idesc_f16(1, 0, 0, kBM, kBN);  // N = 64 queries, M = 128 keys
       constexpr uint32_t idAcc = idesc_f16(1, 0, 1, kD, kBN);   // A TMEM, B MN-major, N = 64
       constexpr uint32_t idDQ = idesc_f16(1, 1, 1, kD, kBM);    // A, B MN-major, M = 64, N = 64
-      const uint32_t sK = smem_u32(smem + kSK), sV = smem_u32(smem + kSV);
-      bool ok = mbar_wait(kv_full, 0, wc, 22);
-      for (int t = 0; t <= n_tiles && ok; ++t) {
-        if (t < n_tiles) {
-          const int sb = t & 1;
-          ok = mbar_wait(&q_full[sb], (t >> 1) & 1, wc, 23);
-          if (ok && t >= 2) ok = mbar_wait(&mma_done[sb], ((t - 2) >> 1) & 1, wc, 24);
+      bool ok = true;
+      int g = 0, i = 0;
+      // the gradient products (dV, dK, dQ) of the previous query tile are issued after the next
+      // tile's S^T / dP^T, so the tensor core works while the pointwise groups run
+      bool have_prev = false;
+      int u_g = 0, u_i = 0;
+      bool u_first = false, u_last = false;
+      auto issue_grads = [&]() -> bool {
+        const int su = u_g & 1;
+        if (!mbar_wait(&wg_full[su], (u_g >> 1) & 1, wc, 25)) return false;
+        if (u_g >= 2 && !mbar_wait(&dq_empty[su], ((u_g - 2) >> 1) & 1, wc, 26)) return false;
+        if (u_first && u_i >= 1 && !mbar_wait(acc_empty, (u_i - 1) & 1, wc, 27)) return false;
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + kSQ + su * 8192), sdO = smem_u32(smem + kSdO + su * 8192);
+        const uint32_t sG = smem_u32(smem + kSG + su * 16384);
+        const uint32_t sK = smem_u32(smem + kSK + (u_i & 1) * 32768);
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns, 2048 B of dO
+          mma_ts(tmem + kTdV, tmem + kTS + su * kBM + kk * 8, sdesc_sw128(sdO + kk * 2048, 8192, 1024), idAcc,
+                 (u_first && kk == 0) ? 0u : 1u);
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk)
+          mma_ts(tmem + kTdK, tmem + kTdP + su * kBM + kk * 8, sdesc_sw128(sQ + kk * 2048, 8192, 1024), idAcc,
+                 (u_first && kk == 0) ? 0u : 1u);
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)  // 16 keys per step: 2048 B of G and of K
+          mma_ss(tmem + kTdQ + su * kD, sdesc_sw128(sG + kk * 2048, 16384, 1024),
+                 sdesc_sw128(sK + kk * 2048, 16384, 1024), idDQ, kk > 0);
+        mma_commit(&q_empty[su]);
+        mma_commit(&dq_full[su]);
+        mma_commit(&mma_done[su]);
+        if (u_last) {
+          mma_commit(acc_full);
+          mma_commit(&kv_empty[u_i & 1]);
+        }
+        have_prev = false;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+        const BwdItem it = bwd_item(p, idx);
+        ok = mbar_wait(&kv_full[i & 1], (i >> 1) & 1, wc, 22);
+        const uint32_t sK = smem_u32(smem + kSK + (i & 1) * 32768), sV = smem_u32(smem + kSV + (i & 1) * 32768);
+        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
+          const int sb = g & 1;
+          ok = mbar_wait(&q_full[sb], (g >> 1) & 1, wc, 23);
+          if (ok && g >= 2) ok = mbar_wait(&mma_done[sb], ((g - 2) >> 1) & 1, wc, 24);
           if (!ok) break;
           tc_fence_after();
           const uint32_t sQ = smem_u32(smem + kSQ + sb * 8192), sdO = smem_u32(smem + kSdO + sb * 8192);
@@ -224,59 +289,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_ss(tmem + kTdP + sb * kBM, sdesc_sw128(sV + kk * 32, 16, 1024),
                    sdesc_sw128(sdO + kk * 32, 16, 1024), idSdP, kk > 0);
           mma_commit(&sdp_full[sb]);
-        }
-        if (t >= 1) {
-          const int u = t - 1, su = u & 1;
-          ok = mbar_wait(&wg_full[su], (u >> 1) & 1, wc, 25);
-          if (ok && u >= 2) ok = mbar_wait(&dq_empty[su], ((u - 2) >> 1) & 1, wc, 26);
+          if (have_prev) ok = issue_grads();
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + kSQ + su * 8192), sdO = smem_u32(smem + kSdO + su * 8192);
-          const uint32_t sG = smem_u32(smem + kSG + su * 16384);
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns, 2048 B of dO
-            mma_ts(tmem + kTdV, tmem + kTS + su * kBM + kk * 8, sdesc_sw128(sdO + kk * 2048, 8192, 1024), idAcc,
-                   (u > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk)
-            mma_ts(tmem + kTdK, tmem + kTdP + su * kBM + kk * 8, sdesc_sw128(sQ + kk * 2048, 8192, 1024), idAcc,
-                   (u > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)  // 16 keys per step: 2048 B of G and of K
-            mma_ss(tmem + kTdQ + su * kD, sdesc_sw128(sG + kk * 2048, 16384, 1024),
-                   sdesc_sw128(sK + kk * 2048, 16384, 1024), idDQ, kk > 0);
-          mma_commit(&q_empty[su]);
-          mma_commit(&dq_full[su]);
-          mma_commit(&mma_done[su]);
+          have_prev = true;
+          u_g = g;
+          u_i = i;
+          u_first = t == 0;
+          u_last = t == it.n_tiles - 1;
         }
       }
-      if (ok) {
-        mma_commit(acc_full);
-      } else {
+      if (ok && have_prev) ok = issue_grads();
+      if (!ok) {
         mma_commit(drain);
         mbar_wait_drain(drain, 0);
       }
     }
     __syncwarp();
-  } else if (warp < 10) {
+  } else {
     // ------------------------------------------------------------------ pointwise (key rows)
     const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;
     const int jr = lg * 32 + lane;  // key row within the tile == TMEM lane
-    const int kj = n0 + jr;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
-    const Map map = BwdMap<Map>::make(p, h);
-    int doc_j = 0;
-    if constexpr (kHasDoc) doc_j = kj < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
     int* docq = reinterpret_cast<int*>(smem + kSDoc) + (wg * 4 + lg) * kBM;
     uint8_t* g_row0 = smem + kSG + jr * 128;
     uint8_t* stg = smem + kSStg + lg * 8192 + wg * 4096;  // this warp's dQ staging (two 16 x 32 boxes)
     const bool leader = elect_one();
-    float g1 = 0.f, g2 = 0.f;
     bool ok = true;
-    // dQ partial of tile u (TMEM buffer wg; an M=64 accumulator keeps rows 16lg..16lg+15 in lanes
-    // 0..15 of this warp's quadrant) -> swizzled staging -> TMA reduce-add into the accumulator
-    auto drain_dq = [&](int u) -> bool {
+    // dQ partial of global query tile u (TMEM buffer wg; an M=64 accumulator keeps rows
+    // 16lg..16lg+15 in lanes 0..15 of this warp's quadrant) -> swizzled staging -> TMA
+    // reduce-add into the fp32 accumulator at row grow
+    auto drain_dq = [&](int u, int grow) -> bool {
       if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[wg], (u >> 1) & 1, wc, 29))) return false;
       tc_fence_after();
       uint32_t r0[32], r1[32];
@@ -303,139 +346,174 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (leader) {
-        const int grow = (int)(bh * p.Tpad + m_first + u * kBM + 16 * lg);
-        tma_reduce_add_2d(&tmDQ, stg, 0, grow);
-        tma_reduce_add_2d(&tmDQ, stg + 2048, 32, grow);
+        tma_reduce_add_2d(&tmDQ, stg, 0, grow + 16 * lg);
+        tma_reduce_add_2d(&tmDQ, stg + 2048, 32, grow + 16 * lg);
         bulk_commit();
       }
       return true;
     };
-    int t_prev = -1;
-    for (int t = wg; t < n_tiles && ok; t += 2) {
-      if (t_prev >= 0) {
-        ok = drain_dq(t_prev);
-        if (!ok) break;
-      }
-      t_prev = t;
-      const int sb = wg;  // == t & 1
-      const int m0 = m_first + t * kBM;
-      if constexpr (kHasDoc) {
-#pragma unroll
-        for (int u = 0; u < kBM / 32; ++u) {
-          const int qi = m0 + u * 32 + lane;
-          docq[u * 32 + lane] = qi < p.T ? p.doc[(int64_t)b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+    int g = 0, i = 0;
+    int prev_g = -1, prev_row = 0;
+    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      const BwdItem it = bwd_item(p, idx);
+      const int64_t bh = (int64_t)it.b * p.H + it.h;
+      const int n0 = it.n0;
+      const int kj = n0 + jr;
+      const Map map = BwdMap<Map>::make(p, it.h);
+      int doc_j = 0;
+      if constexpr (kHasDoc) doc_j = kj < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
+      float g1 = 0.f, g2 = 0.f;
+      for (int t = (wg - g) & 1; t < it.n_tiles && ok; t += 2) {
+        const int gg = g + t;  // gg % 2 == wg
+        const int sb = wg;
+        const int m0 = it.m_first + t * kBM;
+        if (prev_g >= 0) {
+          ok = drain_dq(prev_g, prev_row);
+          if (!ok) break;
         }
-        __syncwarp();
+        prev_g = gg;
+        prev_row = (int)(bh * p.Tpad + m0);
+        if constexpr (kHasDoc) {
+#pragma unroll
+          for (int u = 0; u < kBM / 32; ++u) {
+            const int qi = m0 + u * 32 + lane;
+            docq[u * 32 + lane] = qi < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+          }
+          __syncwarp();
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[sb], (gg >> 1) & 1, wc, 30));
+        if (!ok) break;
+        tc_fence_after();
+        const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
+                          (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
+                          (n0 + kBN <= p.T);
+        // causal diagonal tiles (m0 = n0 or n0 + 64, all keys < T): for query chunk c of warp lg,
+        // with d = 32 c + (m0 - n0) - 32 lg, query column e is valid iff e + d >= lane
+        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 + kBN <= p.T;
+        const float* dl = vdlz + sb * kBM;
+        const float* zi = vzinv + sb * kBM;
+        uint8_t* g_row = g_row0 + sb * 16384;
+#pragma unroll 1
+        for (int c = 0; c < kBM / 32; ++c) {
+          uint32_t wpk[16], gpk[16];
+          const int d = 32 * c + (m0 - n0) - 32 * lg;
+          if (diag && d <= -32) {  // every key of this warp is after every query of the chunk
+#pragma unroll
+            for (int e = 0; e < 16; ++e) wpk[e] = gpk[e] = 0u;
+          } else {
+            uint32_t rs[32], rd[32];
+            tmem_ld32(lane_addr + kTS + sb * kBM + c * 32, rs);
+            tmem_ld32(lane_addr + kTdP + sb * kBM + c * 32, rd);
+            float zc[32], dc[32];  // per-query 1/Z and delta/Z of these 32 columns (shared, broadcast)
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4) {
+              const float4 z4 = reinterpret_cast<const float4*>(zi + c * 32)[v4];
+              const float4 d4 = reinterpret_cast<const float4*>(dl + c * 32)[v4];
+              zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
+              dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+            }
+            tmem_wait_ld();
+            if (full || (diag && d >= 31)) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float wv[2], gv[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const float raw = __uint_as_float(rs[e + u]);
+                  wv[u] = map.prob(raw, true) * zc[e + u];
+                  gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+                }
+                wpk[e / 2] = pack2<true>(wv[0], wv[1]);
+                gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float wv[2], gv[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const int qx = c * 32 + e + u;
+                  bool valid;
+                  if (diag) {
+                    valid = e + u + d >= lane;
+                  } else {
+                    int doc_i = 0;
+                    if constexpr (kHasDoc) doc_i = docq[qx];
+                    valid = pair_valid(m0 + qx, kj, p.T, p.causal, p.window, doc_i, doc_j);
+                  }
+                  const float raw = __uint_as_float(rs[e + u]);
+                  wv[u] = map.prob(raw, valid) * zc[e + u];
+                  gv[u] = map.grad(raw, valid, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+                }
+                wpk[e / 2] = pack2<true>(wv[0], wv[1]);
+                gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+              }
+            }
+          }
+          tmem_st16(lane_addr + kTS + sb * kBM + c * 16, wpk);   // W^T over the consumed S^T columns
+          tmem_st16(lane_addr + kTdP + sb * kBM + c * 16, gpk);  // G^T over the consumed dP^T columns
+          // G (MN-major A operand of dQ): key row jr holds 64 queries = 128 B, 16-byte chunks swizzled
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int chunk = c * 4 + x;
+            *reinterpret_cast<uint4*>(g_row + ((chunk ^ (jr & 7)) << 4)) =
+                make_uint4(gpk[4 * x], gpk[4 * x + 1], gpk[4 * x + 2], gpk[4 * x + 3]);
+          }
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();  // G written by the generic proxy, read by the tensor core
+        tc_fence_before();
+        mbar_arrive(&wg_full[sb]);
       }
-      ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[sb], (t >> 1) & 1, wc, 27));
+      if (!ok) break;
+      // ---- end of the item: dK / dV rows (group 0 stores dV, group 1 stores dK), partials
+      ok = __all_sync(0xffffffffu, mbar_wait(acc_full, i & 1, wc, 31));
       if (!ok) break;
       tc_fence_after();
-      const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
-                        (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
-                        (n0 + kBN <= p.T);
-      const float* dl = vdlz + sb * kBM;
-      const float* zi = vzinv + sb * kBM;
-      uint8_t* g_row = g_row0 + sb * 16384;
-#pragma unroll 1
-      for (int c = 0; c < kBM / 32; ++c) {
-        uint32_t rs[32], rd[32];
-        tmem_ld32(lane_addr + kTS + sb * kBM + c * 32, rs);
-        tmem_ld32(lane_addr + kTdP + sb * kBM + c * 32, rd);
-        float zc[32], dc[32];  // per-query 1/Z and delta/Z of these 32 columns (shared, broadcast)
-#pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4) {
-          const float4 z4 = reinterpret_cast<const float4*>(zi + c * 32)[v4];
-          const float4 d4 = reinterpret_cast<const float4*>(dl + c * 32)[v4];
-          zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
-          dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
-        }
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK), r0);
+        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK) + 32, r1);
         tmem_wait_ld();
-        uint32_t wpk[16], gpk[16];
+        tc_fence_before();
+        mbar_arrive(acc_empty);
+        if (kj < p.T) {
+          __nv_bfloat16* dst = wg == 0 ? p.dv + (int64_t)it.b * p.dv_s0 + (int64_t)it.h * p.dv_s1 + (int64_t)kj * p.dv_s2
+                                       : p.dk + (int64_t)it.b * p.dk_s0 + (int64_t)it.h * p.dk_s1 + (int64_t)kj * p.dk_s2;
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float wv[2], gv[2];
+          for (int v4 = 0; v4 < 4; ++v4)
+            d4[v4] = make_uint4(pack2<true>(__uint_as_float(r0[8 * v4]), __uint_as_float(r0[8 * v4 + 1])),
+                                pack2<true>(__uint_as_float(r0[8 * v4 + 2]), __uint_as_float(r0[8 * v4 + 3])),
+                                pack2<true>(__uint_as_float(r0[8 * v4 + 4]), __uint_as_float(r0[8 * v4 + 5])),
+                                pack2<true>(__uint_as_float(r0[8 * v4 + 6]), __uint_as_float(r0[8 * v4 + 7])));
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int qx = c * 32 + e + u;
-            bool valid = true;
-            if (!full) {
-              int doc_i = 0;
-              if constexpr (kHasDoc) doc_i = docq[qx];
-              valid = pair_valid(m0 + qx, kj, p.T, p.causal, p.window, doc_i, doc_j);
-            }
-            const float raw = __uint_as_float(rs[e + u]);
-            wv[u] = map.prob(raw, valid) * zc[e + u];
-            gv[u] = map.grad(raw, valid, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
-          }
-          wpk[e / 2] = pack2<true>(wv[0], wv[1]);
-          gpk[e / 2] = pack2<true>(gv[0], gv[1]);
-        }
-        tmem_st16(lane_addr + kTS + sb * kBM + c * 16, wpk);   // W^T over the consumed S^T columns
-        tmem_st16(lane_addr + kTdP + sb * kBM + c * 16, gpk);  // G^T over the consumed dP^T columns
-        // G (MN-major A operand of dQ): key row jr holds 64 queries = 128 B, 16-byte chunks swizzled
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const int chunk = c * 4 + x;
-          *reinterpret_cast<uint4*>(g_row + ((chunk ^ (jr & 7)) << 4)) =
-              make_uint4(gpk[4 * x], gpk[4 * x + 1], gpk[4 * x + 2], gpk[4 * x + 3]);
+          for (int v4 = 0; v4 < 4; ++v4)
+            d4[4 + v4] = make_uint4(pack2<true>(__uint_as_float(r1[8 * v4]), __uint_as_float(r1[8 * v4 + 1])),
+                                    pack2<true>(__uint_as_float(r1[8 * v4 + 2]), __uint_as_float(r1[8 * v4 + 3])),
+                                    pack2<true>(__uint_as_float(r1[8 * v4 + 4]), __uint_as_float(r1[8 * v4 + 5])),
+                                    pack2<true>(__uint_as_float(r1[8 * v4 + 6]), __uint_as_float(r1[8 * v4 + 7])));
         }
       }
-      tmem_wait_st();
-      fence_proxy_async_smem();  // G written by the generic proxy, read by the tensor core
-      tc_fence_before();
-      mbar_arrive(&wg_full[sb]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        g1 += __shfl_xor_sync(0xffffffffu, g1, o);
+        g2 += __shfl_xor_sync(0xffffffffu, g2, o);
+      }
+      if (lane == 0) {
+        float* part = p.partials + ((bh * p.n_kv + it.kt) * 8 + (wg * 4 + lg)) * 2;
+        part[0] = g1;
+        part[1] = g2;
+      }
+      g += it.n_tiles;
     }
-    if (ok && t_prev >= 0) ok = drain_dq(t_prev);
+    if (ok && prev_g >= 0) ok = drain_dq(prev_g, prev_row);
     if (leader) bulk_wait<0>();  // every reduce has finished reading shared memory
     __syncwarp();
-    // dK, dV rows: group 0 stores dV, group 1 stores dK
-    if (ok) ok = __all_sync(0xffffffffu, n_tiles == 0 || mbar_wait(acc_full, 0, wc, 28));
-    if (ok) {
-      tc_fence_after();
-      {
-        const int which = wg;
-        __nv_bfloat16* dst = which == 0 ? p.dv + (int64_t)b * p.dv_s0 + (int64_t)h * p.dv_s1 + (int64_t)kj * p.dv_s2
-                                        : p.dk + (int64_t)b * p.dk_s0 + (int64_t)h * p.dk_s1 + (int64_t)kj * p.dk_s2;
-#pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(lane_addr + (which == 0 ? kTdV : kTdK) + c * 32, r);
-          tmem_wait_ld();
-          if (kj < p.T) {
-            uint32_t w[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w[e] = n_tiles == 0 ? 0u : pack2<true>(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) d4[v4] = make_uint4(w[4 * v4], w[4 * v4 + 1], w[4 * v4 + 2], w[4 * v4 + 3]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      g1 += __shfl_xor_sync(0xffffffffu, g1, o);
-      g2 += __shfl_xor_sync(0xffffffffu, g2, o);
-    }
-    if (lane == 0) {
-      red[(wg * 4 + lg) * 2] = g1;
-      red[(wg * 4 + lg) * 2 + 1] = g2;
-    }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float* part = p.partials + (bh * p.n_kv + ktile) * 2;
-    float t1 = 0.f, t2 = 0.f;
-    for (int w = 0; w < 8; ++w) {
-      t1 += red[2 * w];
-      t2 += red[2 * w + 1];
-    }
-    part[0] = t1;
-    part[1] = t2;
-  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -554,8 +632,8 @@ __global__ void bwd_param_kernel(const AuxParams a) {
       const int64_t bhh = (int64_t)b * a.H + hh;
       for (int t = 0; t < nc; ++t) tp += a.prep_part[bhh * nc + t];
       if (a.purified) {
-        const float* part = a.partials + bhh * a.n_kv * 2;
-        for (int t = 0; t < a.n_kv; ++t) {
+        const float* part = a.partials + bhh * a.n_kv * 16;
+        for (int t = 0; t < a.n_kv * 8; ++t) {
           t1 += part[2 * t];
           t2 += part[2 * t + 1];
         }
@@ -599,9 +677,21 @@ WsLayout ws_layout(const Problem& p) {
   w.zinv = align256(w.dlz + BH * Tpad * 4);
   w.dq_acc = align256(w.zinv + BH * Tpad * 4);
   w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
-  w.prep_part = align256(w.partials + BH * n_kv * 2 * 4);
+  w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
   w.total = align256(w.prep_part + BH * (Tpad / 64) * 4);
   return w;
+}
+
+int bwd_num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n = v;
+    else
+      n = 148;
+  }
+  return n;
 }
 
 bool rows16(const Tensor4& t) {  // 16-byte vector row stores of bf16 rows
@@ -618,7 +708,7 @@ int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp, const CU
   const uint32_t smem = kSmemBytes + 1024;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
-  dim3 grid(bp.n_kv, pr.H, pr.B);
+  dim3 grid(std::min(bp.n_items, bwd_num_sms()));
   kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, mdq, bp);
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
@@ -685,6 +775,7 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   bp.dlz = a.dlz; bp.zinv = a.zinv; bp.dq_acc = a.dq_acc;
   bp.partials = reinterpret_cast<float*>(ws + w.partials);
   bp.n_kv = n_kv;
+  bp.n_items = n_kv * pr.B * pr.H;
   bp.status = pr.status;
 
   CUtensorMap mdq;
