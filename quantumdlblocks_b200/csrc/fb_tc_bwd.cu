@@ -52,12 +52,13 @@ constexpr uint32_t kTS = 0, kTdP = 128, kTdV = 256, kTdK = 320, kTdQ = 384;
 // shared memory carve-up (bytes from the 1024-aligned base)
 constexpr uint32_t kSK = 0;                    // K tiles [2 items] 128 x 64 bf16, 32 KB apart (K, V interleaved)
 constexpr uint32_t kSV = 16384;                // V tiles [2 items]
-constexpr uint32_t kSQ = 65536;                // Q stages [2] 64 x 64       8 KB each
-constexpr uint32_t kSdO = 81920;               // dO stages [2]              8 KB each
-constexpr uint32_t kSG = 98304;                // G [2] 128 keys x 64 q      16 KB each
-constexpr uint32_t kSStg = 131072;             // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
-constexpr uint32_t kSVec = 163840;             // dlz[2][64] (delta / Z), zinv[2][64] (1 / Z) fp32
-constexpr uint32_t kSDoc = kSVec + 1024;       // query doc ids [8 warps][64] int32
+constexpr int kQS = 4;                         // Q / dO / vector stages
+constexpr uint32_t kSQ = 65536;                // Q stages [kQS] 64 x 64     8 KB each
+constexpr uint32_t kSdO = 98304;               // dO stages [kQS]            8 KB each
+constexpr uint32_t kSG = 131072;               // G [2] 128 keys x 64 q      16 KB each
+constexpr uint32_t kSStg = 163840;             // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
+constexpr uint32_t kSVec = 196608;             // dlz[kQS][64] (delta / Z), zinv[kQS][64] (1 / Z) fp32
+constexpr uint32_t kSDoc = kSVec + 2048;       // query doc ids [8 warps][64] int32
 constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
 constexpr uint32_t kSmemBytes = kSBar + 256;
 
@@ -134,31 +135,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
   uint64_t* kv_full = bars + 0;    // [2] per item parity
   uint64_t* kv_empty = bars + 2;   // [2]
-  uint64_t* q_full = bars + 4;     // [2] per query-tile parity
-  uint64_t* q_empty = bars + 6;    // [2]
-  uint64_t* sdp_full = bars + 8;   // [2]
-  uint64_t* wg_full = bars + 10;   // [2]
-  uint64_t* mma_done = bars + 12;  // [2]
-  uint64_t* dq_full = bars + 14;   // [2]
-  uint64_t* dq_empty = bars + 16;  // [2]
-  uint64_t* acc_full = bars + 18;
-  uint64_t* acc_empty = bars + 19;
-  uint64_t* drain = bars + 20;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 22);
-  float* vdlz = reinterpret_cast<float*>(smem + kSVec);          // [2][64]
-  float* vzinv = reinterpret_cast<float*>(smem + kSVec + 512);   // [2][64]
+  uint64_t* q_full = bars + 4;     // [kQS] per query-tile stage
+  uint64_t* q_empty = bars + 8;    // [kQS]
+  uint64_t* sdp_full = bars + 12;  // [2] per query-tile parity
+  uint64_t* wg_full = bars + 14;   // [2]
+  uint64_t* mma_done = bars + 16;  // [2]
+  uint64_t* dq_full = bars + 18;   // [2]
+  uint64_t* dq_empty = bars + 20;  // [2]
+  uint64_t* acc_full = bars + 22;
+  uint64_t* acc_empty = bars + 23;
+  uint64_t* drain = bars + 24;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 26);
+  float* vdlz = reinterpret_cast<float*>(smem + kSVec);                // [kQS][64]
+  float* vzinv = reinterpret_cast<float*>(smem + kSVec + kQS * 256);   // [kQS][64]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx wc{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < kQS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&sdp_full[i], 1);
       mbar_init(&wg_full[i], 128);
       mbar_init(&mma_done[i], 1);
@@ -206,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t bh = (int64_t)it.b * p.H + it.h;
         if (kv_issued <= i) ok = load_kv(i, it);
         for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
-          const int st = g & 1;
-          if (g >= 2) ok = mbar_wait(&q_empty[st], ((g >> 1) - 1) & 1, wc, 21);
+          const int st = g % kQS;
+          if (g >= kQS) ok = mbar_wait(&q_empty[st], ((g / kQS) - 1) & 1, wc, 21);
           if (!ok) break;
           const int m0 = it.m_first + t * kBM;
           mbar_arrive_expect_tx(&q_full[st], 2 * kBM * kD * 2 + 2 * kBM * 4);
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        for (int gg = max(0, g - 2); gg < g; ++gg) mbar_wait_drain(&q_full[gg & 1], (gg >> 1) & 1);
+        for (int gg = max(0, g - kQS); gg < g; ++gg) mbar_wait_drain(&q_full[gg % kQS], (gg / kQS) & 1);
         for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_wait_drain(&kv_full[ii & 1], (ii >> 1) & 1);
       }
     }
@@ -244,22 +247,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (u_g >= 2 && !mbar_wait(&dq_empty[su], ((u_g - 2) >> 1) & 1, wc, 26)) return false;
         if (u_first && u_i >= 1 && !mbar_wait(acc_empty, (u_i - 1) & 1, wc, 27)) return false;
         tc_fence_after();
-        const uint32_t sQ = smem_u32(smem + kSQ + su * 8192), sdO = smem_u32(smem + kSdO + su * 8192);
-        const uint32_t sG = smem_u32(smem + kSG + su * 16384);
-        const uint32_t sK = smem_u32(smem + kSK + (u_i & 1) * 32768);
+        const int qs = u_g % kQS;
+        // descriptors built once per operand; each K step adds its byte offset / 16 to the start
+        // address field (addresses stay below 256 KB, so the 14-bit field never carries)
+        const uint64_t dQmn = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 8192, 1024);
+        const uint64_t ddOmn = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 8192, 1024);
+        const uint64_t dG = sdesc_sw128(smem_u32(smem + kSG + su * 16384), 16384, 1024);
+        const uint64_t dKmn = sdesc_sw128(smem_u32(smem + kSK + (u_i & 1) * 32768), 16384, 1024);
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns, 2048 B of dO
-          mma_ts(tmem + kTdV, tmem + kTS + su * kBM + kk * 8, sdesc_sw128(sdO + kk * 2048, 8192, 1024), idAcc,
-                 (u_first && kk == 0) ? 0u : 1u);
+          mma_ts(tmem + kTdV, tmem + kTS + su * kBM + kk * 8, ddOmn + kk * 128, idAcc, (u_first && kk == 0) ? 0u : 1u);
 #pragma unroll
         for (int kk = 0; kk < kBM / 16; ++kk)
-          mma_ts(tmem + kTdK, tmem + kTdP + su * kBM + kk * 8, sdesc_sw128(sQ + kk * 2048, 8192, 1024), idAcc,
-                 (u_first && kk == 0) ? 0u : 1u);
+          mma_ts(tmem + kTdK, tmem + kTdP + su * kBM + kk * 8, dQmn + kk * 128, idAcc, (u_first && kk == 0) ? 0u : 1u);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)  // 16 keys per step: 2048 B of G and of K
-          mma_ss(tmem + kTdQ + su * kD, sdesc_sw128(sG + kk * 2048, 16384, 1024),
-                 sdesc_sw128(sK + kk * 2048, 16384, 1024), idDQ, kk > 0);
-        mma_commit(&q_empty[su]);
+          mma_ss(tmem + kTdQ + su * kD, dG + kk * 128, dKmn + kk * 128, idDQ, kk > 0);
+        mma_commit(&q_empty[qs]);
         mma_commit(&dq_full[su]);
         mma_commit(&mma_done[su]);
         if (u_last) {
@@ -272,22 +276,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
         const BwdItem it = bwd_item(p, idx);
         ok = mbar_wait(&kv_full[i & 1], (i >> 1) & 1, wc, 22);
-        const uint32_t sK = smem_u32(smem + kSK + (i & 1) * 32768), sV = smem_u32(smem + kSV + (i & 1) * 32768);
+        const uint64_t dK = sdesc_sw128(smem_u32(smem + kSK + (i & 1) * 32768), 16, 1024);
+        const uint64_t dV = sdesc_sw128(smem_u32(smem + kSV + (i & 1) * 32768), 16, 1024);
         for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
           const int sb = g & 1;
-          ok = mbar_wait(&q_full[sb], (g >> 1) & 1, wc, 23);
+          const int qs = g % kQS;
+          ok = mbar_wait(&q_full[qs], (g / kQS) & 1, wc, 23);
           if (ok && g >= 2) ok = mbar_wait(&mma_done[sb], ((g - 2) >> 1) & 1, wc, 24);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t sQ = smem_u32(smem + kSQ + sb * 8192), sdO = smem_u32(smem + kSdO + sb * 8192);
+          const uint64_t dQ = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 16, 1024);
+          const uint64_t ddO = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements per step: 32 B along the row
+            mma_ss(tmem + kTS + sb * kBM, dK + kk * 2, dQ + kk * 2, idSdP, kk > 0);
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
-            mma_ss(tmem + kTS + sb * kBM, sdesc_sw128(sK + kk * 32, 16, 1024), sdesc_sw128(sQ + kk * 32, 16, 1024),
-                   idSdP, kk > 0);
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_ss(tmem + kTdP + sb * kBM, sdesc_sw128(sV + kk * 32, 16, 1024),
-                   sdesc_sw128(sdO + kk * 32, 16, 1024), idSdP, kk > 0);
+            mma_ss(tmem + kTdP + sb * kBM, dV + kk * 2, ddO + kk * 2, idSdP, kk > 0);
           mma_commit(&sdp_full[sb]);
           if (have_prev) ok = issue_grads();
           if (!ok) break;
@@ -390,11 +395,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         // causal diagonal tiles (m0 = n0 or n0 + 64, all keys < T): for query chunk c of warp lg,
         // with d = 32 c + (m0 - n0) - 32 lg, query column e is valid iff e + d >= lane
         const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 + kBN <= p.T;
-        const float* dl = vdlz + sb * kBM;
-        const float* zi = vzinv + sb * kBM;
+        const float* dl = vdlz + (gg % kQS) * kBM;
+        const float* zi = vzinv + (gg % kQS) * kBM;
         uint8_t* g_row = g_row0 + sb * 16384;
+        const uint32_t s_col = lane_addr + kTS + sb * kBM, p_col = lane_addr + kTdP + sb * kBM;
+        // one 16-query sub-chunk of a fully valid tile: W, G -> TMEM (over consumed columns), G -> smem
+        auto sub16 = [&](int sc, const uint32_t (&rs)[16], const uint32_t (&rd)[16]) {
+          float zc[16], dc[16];
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 z4 = reinterpret_cast<const float4*>(zi + sc * 16)[v4];
+            const float4 d4 = reinterpret_cast<const float4*>(dl + sc * 16)[v4];
+            zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
+            dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+          }
+          uint32_t wpk[8], gpk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float wv[2], gv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float raw = __uint_as_float(rs[e + u]);
+              wv[u] = map.prob(raw, true) * zc[e + u];
+              gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+            }
+            wpk[e / 2] = pack2<true>(wv[0], wv[1]);
+            gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+          }
+          tmem_st8(s_col + sc * 8, wpk);
+          tmem_st8(p_col + sc * 8, gpk);
+          *reinterpret_cast<uint4*>(g_row + (((2 * sc) ^ (jr & 7)) << 4)) = make_uint4(gpk[0], gpk[1], gpk[2], gpk[3]);
+          *reinterpret_cast<uint4*>(g_row + (((2 * sc + 1) ^ (jr & 7)) << 4)) = make_uint4(gpk[4], gpk[5], gpk[6], gpk[7]);
+        };
+        if (full) {
+          // software pipeline: the TMEM loads of sub-chunk s+1 are in flight while s is computed
+          uint32_t sA[16], dA[16], sB[16], dB[16];
+          tmem_ld16(s_col, sA);
+          tmem_ld16(p_col, dA);
+          tmem_wait_ld();
+#pragma unroll
+          for (int sc = 0; sc < kBM / 16; sc += 2) {
+            tmem_ld16(s_col + (sc + 1) * 16, sB);
+            tmem_ld16(p_col + (sc + 1) * 16, dB);
+            sub16(sc, sA, dA);
+            tmem_wait_ld();
+            if (sc + 2 < kBM / 16) {
+              tmem_ld16(s_col + (sc + 2) * 16, sA);
+              tmem_ld16(p_col + (sc + 2) * 16, dA);
+            }
+            sub16(sc + 1, sB, dB);
+            tmem_wait_ld();
+          }
+        }
 #pragma unroll 1
-        for (int c = 0; c < kBM / 32; ++c) {
+        for (int c = 0; c < (full ? 0 : kBM / 32); ++c) {
           uint32_t wpk[16], gpk[16];
           const int d = 32 * c + (m0 - n0) - 32 * lg;
           if (diag && d <= -32) {  // every key of this warp is after every query of the chunk
@@ -413,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
             }
             tmem_wait_ld();
-            if (full || (diag && d >= 31)) {
+            if (diag && d >= 31) {
 #pragma unroll
               for (int e = 0; e < 32; e += 2) {
                 float wv[2], gv[2];
