@@ -601,48 +601,60 @@ struct AuxParams {
   int scale_per_head, tau_per_head;
 };
 
-// One block per (64-row chunk, head, batch); each warp handles 8 rows: delta_i / Z_i, 1 / Z_i,
-// a zeroed dQ accumulator row, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
-// dscale / d gamma).
+// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id),
+// a zeroed dQ accumulator chunk, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
+// dscale / d gamma).  Eight lanes share a row (8 elements = 16 bytes of bf16 each), so a warp
+// reads four 128-byte rows per load instruction.
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3, part = lane & 7;  // row within the group of 4, 8-element slice
   const int64_t bh = (int64_t)b * a.H + h;
   __shared__ float csum_w[8];
   float csum = 0.f;
-#pragma unroll 4
-  for (int r = 0; r < 8; ++r) {
-    const int i = chunk * 64 + warp * 8 + r;
+#pragma unroll
+  for (int r4 = 0; r4 < 2; ++r4) {
+    const int i = chunk * 64 + warp * 8 + r4 * 4 + sub;
     const int64_t row = bh * a.Tpad + i;
     float s = 0.f;
     if (i < a.T) {
-      for (int d = 2 * lane; d < a.D; d += 64) {  // two adjacent elements per lane
-        const int64_t oo = (int64_t)b * a.o_s0 + (int64_t)h * a.o_s1 + (int64_t)i * a.o_s2 + (int64_t)d * a.o_s3;
-        const int64_t od = (int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 + (int64_t)d * a.do_s3;
-        float o0, o1;
-        if (a.out_f32) {
-          const float* op = reinterpret_cast<const float*>(a.out) + oo;
-          o0 = op[0];
-          o1 = op[a.o_s3];
-        } else {
-          const __nv_bfloat16* op = reinterpret_cast<const __nv_bfloat16*>(a.out) + oo;
-          o0 = __bfloat162float(op[0]);
-          o1 = __bfloat162float(op[a.o_s3]);
+      const int d0 = part * 8;
+      const __nv_bfloat16* dop = a.dout + (int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 + d0;
+      const uint4 dv = *reinterpret_cast<const uint4*>(dop);
+      float o[8];
+      const int64_t oo = (int64_t)b * a.o_s0 + (int64_t)h * a.o_s1 + (int64_t)i * a.o_s2 + d0;
+      if (a.out_f32) {
+        const float4 x = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[0];
+        const float4 y = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[1];
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
+      } else {
+        const uint4 ov = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out) + oo);
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          o[2 * x] = sm100::bf16_lo(ow[x]);
+          o[2 * x + 1] = sm100::bf16_hi(ow[x]);
         }
-        s += o0 * __bfloat162float(a.dout[od]) + o1 * __bfloat162float(a.dout[od + a.do_s3]);
       }
+      const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int x = 0; x < 4; ++x) s += o[2 * x] * sm100::bf16_lo(dw[x]) + o[2 * x + 1] * sm100::bf16_hi(dw[x]);
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) {
+    for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (part == 0) {
       const float zi = i < a.T ? 1.f / a.z[bh * a.T + i] : 0.f;
       a.dlz[row] = s * zi;
       a.zinv[row] = zi;
       csum += a.eps * s * zi;
     }
-    float2* acc = reinterpret_cast<float2*>(a.dq_acc + row * a.D);
-    for (int d = lane; d < a.D / 2; d += 32) acc[d] = make_float2(0.f, 0.f);
   }
+  // zero this chunk's 64 accumulator rows (64 x 64 fp32 = 16 KB, one float4 per thread x 4)
+  float4* acc = reinterpret_cast<float4*>(a.dq_acc + (bh * a.Tpad + chunk * 64) * a.D);
+#pragma unroll
+  for (int x = 0; x < 4; ++x) acc[x * 256 + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, off);
   if (lane == 0) csum_w[warp] = csum;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -677,47 +689,60 @@ __global__ void __launch_bounds__(256) bwd_post_kernel(const AuxParams a) {
 //   plain     dscale_h = (2 / scale_h) sum_{b,i} eps delta_i / Z_i
 //   purified  dgamma_h = (4 / gamma_h) (sum_{b,i} eps delta_i / Z_i - sum eps_base b^2 dP),
 //             dtau_h   = sum -4 u^3 dP gamma        (the last two from the main kernel's partials)
-__global__ void bwd_param_kernel(const AuxParams a) {
-  const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  auto head_terms = [&](int hh, float& d1, float& d2) {
-    float tp = 0.f, t1 = 0.f, t2 = 0.f;
-    const int nc = a.Tpad / 64;
-    for (int b = 0; b < a.B; ++b) {
-      const int64_t bhh = (int64_t)b * a.H + hh;
-      for (int t = 0; t < nc; ++t) tp += a.prep_part[bhh * nc + t];
-      if (a.purified) {
-        const float* part = a.partials + bhh * a.n_kv * 16;
-        for (int t = 0; t < a.n_kv * 8; ++t) {
-          t1 += part[2 * t];
-          t2 += part[2 * t + 1];
-        }
+// One block per head: each thread sums a fixed strided subset, then a fixed-shape tree; block 0
+// also folds the heads together for shared (scalar) parameters after a second pass.
+__global__ void __launch_bounds__(256) bwd_param_kernel(const AuxParams a, float* head_terms) {
+  const int h = blockIdx.x;
+  const int nc = a.Tpad / 64;
+  __shared__ float r1[256], r2[256], rp[256];
+  float tp = 0.f, t1 = 0.f, t2 = 0.f;
+  for (int b = 0; b < a.B; ++b) {
+    const int64_t bhh = (int64_t)b * a.H + h;
+    for (int t = threadIdx.x; t < nc; t += 256) tp += a.prep_part[bhh * nc + t];
+    if (a.purified) {
+      const float* part = a.partials + bhh * a.n_kv * 16;
+      for (int t = threadIdx.x; t < a.n_kv * 8; t += 256) {
+        t1 += part[2 * t];
+        t2 += part[2 * t + 1];
       }
     }
-    const float sc = a.scale[a.scale_per_head ? hh : 0];
-    d1 = a.purified ? (4.f / sc) * (tp - t1) : (2.f / sc) * tp;
-    d2 = t2;
-  };
-  if (h < a.H) {
-    float d1, d2;
-    head_terms(h, d1, d2);
+  }
+  rp[threadIdx.x] = tp;
+  r1[threadIdx.x] = t1;
+  r2[threadIdx.x] = t2;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      rp[threadIdx.x] += rp[threadIdx.x + w];
+      r1[threadIdx.x] += r1[threadIdx.x + w];
+      r2[threadIdx.x] += r2[threadIdx.x + w];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float sc = a.scale[a.scale_per_head ? h : 0];
+    const float d1 = a.purified ? (4.f / sc) * (rp[0] - r1[0]) : (2.f / sc) * rp[0];
+    const float d2 = r2[0];
     if (a.scale_per_head) a.dscale[h] += d1;
     if (a.dtau != nullptr && a.tau_per_head) a.dtau[h] += d2;
-  }
-  if (h == 0 && (!a.scale_per_head || (a.dtau != nullptr && !a.tau_per_head))) {
-    float s1 = 0.f, s2 = 0.f;
-    for (int hh = 0; hh < a.H; ++hh) {
-      float d1, d2;
-      head_terms(hh, d1, d2);
-      s1 += d1;
-      s2 += d2;
-    }
-    if (!a.scale_per_head) a.dscale[0] += s1;
-    if (a.dtau != nullptr && !a.tau_per_head) a.dtau[0] += s2;
+    head_terms[2 * h] = d1;
+    head_terms[2 * h + 1] = d2;
   }
 }
 
+// shared (scalar) scale / tau: the per-head terms added in head order
+__global__ void bwd_param_shared_kernel(const AuxParams a, const float* head_terms) {
+  float s1 = 0.f, s2 = 0.f;
+  for (int hh = 0; hh < a.H; ++hh) {
+    s1 += head_terms[2 * hh];
+    s2 += head_terms[2 * hh + 1];
+  }
+  if (!a.scale_per_head) a.dscale[0] += s1;
+  if (a.dtau != nullptr && !a.tau_per_head) a.dtau[0] += s2;
+}
+
 struct WsLayout {
-  size_t dlz, zinv, dq_acc, partials, prep_part, total;
+  size_t dlz, zinv, dq_acc, partials, prep_part, head_terms, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -732,7 +757,8 @@ WsLayout ws_layout(const Problem& p) {
   w.dq_acc = align256(w.zinv + BH * Tpad * 4);
   w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
   w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
-  w.total = align256(w.prep_part + BH * (Tpad / 64) * 4);
+  w.head_terms = align256(w.prep_part + BH * (Tpad / 64) * 4);
+  w.total = align256(w.head_terms + (size_t)p.H * 2 * 4);
   return w;
 }
 
@@ -776,6 +802,11 @@ bool tc_bwd_supported(const Problem& p) {
   if (p.out_dtype != FB_BF16 && p.out_dtype != FB_F32) return false;
   if (!tma_ok(p.q) || !tma_ok(p.k) || !tma_ok(p.v) || !tma_ok(p.dout)) return false;
   if (!rows16(p.dq) || !rows16(p.dk) || !rows16(p.dv)) return false;
+  // the pre-pass reads O rows as 16-byte vectors
+  const int oelt = p.out_dtype == FB_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(p.o.ptr) & 15) != 0 || p.o.s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((p.o.s[i] * oelt) % 16 != 0) return false;
   return true;
 }
 
@@ -847,10 +878,16 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (rc != FB_OK) return rc;
   const int64_t post_threads = (int64_t)pr.B * pr.H * pr.T * (pr.D / 8);
   bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
-  bwd_param_kernel<<<(pr.H + 127) / 128, 128, 0, s>>>(a);
+  float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
+  bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
+  int n = 4;
+  if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
+    bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
+    ++n;
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
-  *launches = 4;
+  *launches = n;
   return FB_OK;
 }
 
