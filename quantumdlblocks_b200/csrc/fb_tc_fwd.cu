@@ -8,13 +8,19 @@
 // per-item set-up latency is hidden.  Warp-specialised pipeline (320 threads):
 //
 //   warp 0      TMA producer: Q of an item (double-buffered, the next item's Q is fetched
-//               while the current one runs), K_j and V_j through a ring of kStages stages
-//               with separate K and V barriers (S_j needs only K_j)
+//               while the current one runs), K_j and V_j through rings of kStages stages with
+//               separate full and empty barriers: a K stage is released when S_j completes, a V
+//               stage when O += P_j V_j does, and V runs one tile behind K in the issue order, so
+//               K_{j+kStages} is requested about one tile earlier than a shared K/V stage allows
 //   warp 1      TMEM owner + MMA issuer (one elected lane):
 //                 S_g = Q K_g^T      tcgen05.mma kind::f16, A = Q (smem, K-major),
 //                                    B = K_g (smem, K-major), D = S[g%2] in TMEM (fp32)
 //                 O  += P_g V_g      A = P[g%2] (TMEM, bf16 packed), B = V_g (smem, MN-major),
-//                                    D = O in TMEM (fp32); the first tile of an item overwrites O
+//                                    D = O in TMEM (fp32); the first tile of an item overwrites O.
+//                                    For d=64 the same MMA also produces the row sums: N = 80,
+//                                    and the B columns 64..79 are a ones tile in shared memory
+//                                    (reached through the descriptor's leading-byte offset), so
+//                                    TMEM columns O[64..80) accumulate Z = P 1.
 //               S_{g+1} is issued before O += P_g V_g so the tensor core works while the
 //               pointwise warps turn S_g into P_g.
 //   warps 2-9   two pointwise ("Born") warpgroups; group w handles the tiles with g % 2 == w
@@ -31,7 +37,7 @@
 // without the bf16 rounding of p (which the 2/a factor of dS would otherwise amplify).
 //
 // TMEM columns (512): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384) O [384,384+D);
-// for d=64 also Z [448,464): the row sums, produced by the tensor core as P times a ones tile.
+// for d=64 also Z [448,464) right after O: the row sums, produced by the PV product itself.
 #include <cuda.h>
 
 #include <algorithm>
@@ -52,8 +58,9 @@ constexpr uint32_t kTmemCols = 512;
 template <int D>
 struct FwdCfg {
   static constexpr int kStages = D == 64 ? 5 : 2;
-  // d=64: Z comes from the tensor core (P times a ones tile into 16 spare TMEM columns); d=128
-  // has no spare columns and sums Z in the pointwise warps
+  // d=64: Z comes from the tensor core (the PV product is widened to N = 80 with a ones block
+  // as the extra B columns, into the 16 TMEM columns after O); d=128 has no spare columns and
+  // sums Z in the pointwise warps
   static constexpr bool kTcZ = D == 64;
   static constexpr int kHalves = D / 64;                // 64-column halves of a head
   static constexpr uint32_t kTileBytes = kBN * D * 2;   // one K or V tile (== one Q tile)
@@ -61,12 +68,15 @@ struct FwdCfg {
   static constexpr uint32_t kQOff = 0;                  // Q[2]
   static constexpr uint32_t kKOff = 2 * kTileBytes;
   static constexpr uint32_t kVOff = kKOff + kStages * kTileBytes;
-  static constexpr uint32_t kOnesOff = kVOff + kStages * kTileBytes;  // 16 rows x 128 B of bf16 ones
+  // 16 rows x 128 B of bf16 ones; above every V stage, so the leading-byte offset from a V
+  // sub-tile to it is positive
+  static constexpr uint32_t kOnesOff = kVOff + kStages * kTileBytes;
   static constexpr uint32_t kBarOff = kOnesOff + 2048;
   static constexpr uint32_t kDocOff = kBarOff + 512;             // [8 warps][kBN] int32
   static constexpr uint32_t kZOff = kDocOff + 8 * kBN * 4;         // [2 items][2 groups][kBM] fp32
   static constexpr uint32_t kSmemBytes = kZOff + 4 * kBM * 4;
   static constexpr uint32_t kTmemS = 0, kTmemP = 256, kTmemO = 384, kTmemZ = 448;
+  static_assert(!kTcZ || kTmemZ == kTmemO + D, "Z columns follow O: one N = D + 16 product writes both");
 };
 
 struct FwdParams {
@@ -131,16 +141,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* q_empty = bars + 2;          // [2]
   uint64_t* k_full = bars + 4;           // [S]
   uint64_t* v_full = bars + 4 + S;       // [S]
-  uint64_t* kv_empty = bars + 4 + 2 * S; // [S]
-  uint64_t* s_full = bars + 4 + 3 * S;   // [2]
-  uint64_t* p_full = bars + 6 + 3 * S;   // [2]
-  uint64_t* pv_done = bars + 8 + 3 * S;  // [2]
-  uint64_t* o_full = bars + 10 + 3 * S;
-  uint64_t* o_empty = bars + 11 + 3 * S;
-  uint64_t* z_bar = bars + 12 + 3 * S;
-  uint64_t* drain = bars + 13 + 3 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 33);
+  uint64_t* k_empty = bars + 4 + 2 * S;  // [S]
+  uint64_t* v_empty = bars + 4 + 3 * S;  // [S]
+  uint64_t* s_full = bars + 4 + 4 * S;   // [2]
+  uint64_t* p_full = bars + 6 + 4 * S;   // [2]
+  uint64_t* pv_done = bars + 8 + 4 * S;  // [2]
+  uint64_t* o_full = bars + 10 + 4 * S;
+  uint64_t* o_empty = bars + 11 + 4 * S;
+  uint64_t* z_bar = bars + 12 + 4 * S;
+  uint64_t* drain = bars + 13 + 4 * S;
+  static_assert(14 + 4 * S <= 48, "barrier area");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 48);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 49);
   int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);
   float* zpart = reinterpret_cast<float*>(smem + Cfg::kZOff);
 
@@ -159,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int st = 0; st < S; ++st) {
       mbar_init(&k_full[st], 1);
       mbar_init(&v_full[st], 1);
-      mbar_init(&kv_empty[st], 1);
+      mbar_init(&k_empty[st], 1);
+      mbar_init(&v_empty[st], 1);
     }
     mbar_init(o_full, 1);
     mbar_init(o_empty, 256);
@@ -191,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ TMA producer
     if (elect_one()) {
       bool ok = true;
-      int g = 0, i = 0, q_issued = 0;
+      int g = 0, i = 0, q_issued = 0, v_issued = 0;
+      int vb = 0, vh = 0, vn0 = 0;  // coordinates of the V tile still to be requested (tile v_issued)
       auto load_q = [&](int item_seq, const Item& it) -> bool {
         const int qb = item_seq & 1;
         if (item_seq >= 2 && !mbar_wait(&q_empty[qb], ((item_seq >> 1) - 1) & 1, wc, 1)) return false;
@@ -203,12 +217,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         q_issued = item_seq + 1;
         return true;
       };
+      // V of tile v_issued, once O += P V of the tile kStages earlier has released its stage
+      auto load_v = [&]() -> bool {
+        const int vs = v_issued % S;
+        if (v_issued >= S && !mbar_wait(&v_empty[vs], ((v_issued / S) - 1) & 1, wc, 12)) return false;
+        mbar_arrive_expect_tx(&v_full[vs], Cfg::kTileBytes);
+#pragma unroll
+        for (int hf = 0; hf < Cfg::kHalves; ++hf)
+          tma_load_4d(smem + Cfg::kVOff + vs * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmV, &v_full[vs], hf * 64,
+                      vn0, vh, vb);
+        ++v_issued;
+        return true;
+      };
       for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
         const Item it = item_at(p, idx);
         if (q_issued <= i) ok = load_q(i, it);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
           const int st = g % S;
-          if (g >= S) ok = mbar_wait(&kv_empty[st], ((g / S) - 1) & 1, wc, 2);
+          if (g >= S) ok = mbar_wait(&k_empty[st], ((g / S) - 1) & 1, wc, 2);
           if (!ok) break;
           const int n0 = it.n_first + t * kBN;
           mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
@@ -216,21 +242,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int hf = 0; hf < Cfg::kHalves; ++hf)
             tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmK, &k_full[st], hf * 64,
                         n0, it.h, it.b);
-          mbar_arrive_expect_tx(&v_full[st], Cfg::kTileBytes);
-#pragma unroll
-          for (int hf = 0; hf < Cfg::kHalves; ++hf)
-            tma_load_4d(smem + Cfg::kVOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmV, &v_full[st], hf * 64,
-                        n0, it.h, it.b);
-          // once the first K/V of this item is on its way, fetch the next item's Q
+          if (v_issued < g) ok = load_v();  // V of the previous tile
+          if (!ok) break;
+          vb = it.b;
+          vh = it.h;
+          vn0 = n0;
+          // once the first K of this item is on its way, fetch the next item's Q
           if (t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_q(i + 1, item_at(p, idx + gridDim.x));
         }
       }
+      if (ok && v_issued < g) ok = load_v();  // V of the last tile
       if (!ok) {
-        // abandoned: let the copies already in flight land before the CTA exits
-        for (int gg = max(0, g - S); gg < g; ++gg) {
-          mbar_wait_drain(&k_full[gg % S], (gg / S) & 1);
-          mbar_wait_drain(&v_full[gg % S], (gg / S) & 1);
-        }
+        // abandoned: let the copies already in flight land before the CTA exits (g K tiles and
+        // v_issued V tiles were requested)
+        for (int gg = max(0, g - S); gg < g; ++gg) mbar_wait_drain(&k_full[gg % S], (gg / S) & 1);
+        for (int gg = max(0, v_issued - S); gg < v_issued; ++gg) mbar_wait_drain(&v_full[gg % S], (gg / S) & 1);
         for (int qq = max(0, q_issued - 2); qq < q_issued; ++qq) mbar_wait_drain(&q_full[qq & 1], (qq >> 1) & 1);
       }
     }
@@ -239,8 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t idS = idesc_f16(1, 0, 0, kBN, kBM);  // S: A K-major, B K-major, N = 128
-      constexpr uint32_t idO = idesc_f16(1, 0, 1, D, kBM);    // O: A TMEM, B MN-major, N = D
-      constexpr uint32_t idZ = idesc_f16(1, 0, 1, 16, kBM);   // Z: A TMEM (P), B = ones, N = 16
+      // O (and for d=64 Z): A TMEM, B MN-major, N = D (+16 ones columns)
+      constexpr uint32_t idO = idesc_f16(1, 0, 1, Cfg::kTcZ ? D + 16 : D, kBM);
       const uint32_t ones_base = smem_u32(smem + Cfg::kOnesOff);
       bool ok = true;
       int g = 0, i = 0;
@@ -257,18 +283,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_p = tmem + Cfg::kTmemP + (pv_g & 1) * (kBN / 2);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
-          // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile
-          mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(v_base + kk * 2048, Cfg::kHalfBytes, 1024), idO,
-                 (pv_first && kk == 0) ? 0u : 1u);
+          // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile.
+          // The leading-byte offset is the distance to the next 64-column block of B: the second
+          // half of V for d=128; for d=64 the ones tile (every B row of it is ones, whatever the
+          // swizzle, so each K step may read the same 2 KB)
+          const uint32_t sub = v_base + kk * 2048;
+          const uint32_t lbo = Cfg::kTcZ ? ones_base - sub : Cfg::kHalfBytes;
+          mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(sub, lbo, 1024), idO, (pv_first && kk == 0) ? 0u : 1u);
         }
-        if constexpr (Cfg::kTcZ) {
-          // Z += P 1: every B row is ones, so each K step reads the same 16-row ones tile
-#pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_ts(tmem + Cfg::kTmemZ, a_p + kk * 8, sdesc_sw128(ones_base, 1024, 1024), idZ,
-                   (pv_first && kk == 0) ? 0u : 1u);
-        }
-        mma_commit(&kv_empty[pv_st]);
+        mma_commit(&v_empty[pv_st]);
         mma_commit(&pv_done[pv_g & 1]);
         if (pv_last) mma_commit(o_full);
         have_prev = false;
@@ -292,6 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_ss(d_s, sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024), idS, kk > 0);
           }
           mma_commit(&s_full[g & 1]);
+          mma_commit(&k_empty[st]);
           if (t == it.n_count - 1) mma_commit(&q_empty[i & 1]);
           if (have_prev) ok = issue_pv();
           if (!ok) break;
@@ -321,12 +345,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t p_addr = lane_addr + Cfg::kTmemP + wg * (kBN / 2);
     bool ok = true;
     int g = 0, i = 0;
+    // Per-item parameters (score map, this row's document id) come from global memory; those of
+    // the next item are requested before the current item's epilogue, which hides their latency.
+    Item it_n{};
+    Map map_n{};
+    int doc_n = 0;
+    auto fetch = [&](int idx) {
+      it_n = item_at(p, idx);
+      map_n = TcMap<Map>::make(p, it_n.h);
+      if constexpr (kHasDoc) {
+        const int q = it_n.m0 + row;
+        doc_n = q < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)q * p.doc_s1] : -1;
+      }
+    };
+    if (blockIdx.x < p.n_items) fetch(blockIdx.x);
     for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
-      const Item it = item_at(p, idx);
+      const Item it = it_n;
+      const Map map = map_n;
+      const int doc_i = doc_n;
       const int qi = it.m0 + row;
-      const Map map = TcMap<Map>::make(p, it.h);
-      int doc_i = 0;
-      if constexpr (kHasDoc) doc_i = qi < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+      (void)doc_i;
       float zsum = 0.f;
       for (int t = (wg - g) & 1; t < it.n_count && ok; t += 2) {
         const int gg = g + t;  // gg % 2 == wg
@@ -423,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&p_full[wg]);
       }
+      if (idx + (int)gridDim.x < p.n_items) fetch(idx + gridDim.x);
       // ---- epilogue of the item: Z (tensor-core sum, or the two groups' row sums), O * (1 / Z)
       float* zp = zpart + (i & 1) * 2 * kBM;
       if constexpr (!Cfg::kTcZ) {
