@@ -3,8 +3,9 @@
 // Three launches (all on the caller's stream):
 //   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
 //                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
-//   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile),
-//                        heaviest first; each item walks the 64-query tiles that can hold valid
+//   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
+//                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
+//                        tiles that can hold valid
 //                        pairs and accumulates dK, dV in TMEM; dQ partials are reduced into the
 //                        fp32 accumulator with TMA tensor reduce-add.  The query-tile pipeline
 //                        runs on across items (K, V double-buffered per item)
@@ -54,13 +55,14 @@ constexpr uint32_t kSK = 0;                    // K tiles [2 items] 128 x 64 bf1
 constexpr uint32_t kSV = 16384;                // V tiles [2 items]
 constexpr int kQS = 4;                         // Q / dO / vector stages
 constexpr uint32_t kSQ = 65536;                // Q stages [kQS] 64 x 64     8 KB each
-constexpr uint32_t kSdO = 98304;               // dO stages [kQS]            8 KB each
-constexpr uint32_t kSG = 131072;               // G [2] 128 keys x 64 q      16 KB each
-constexpr uint32_t kSStg = 163840;             // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
-constexpr uint32_t kSVec = 196608;             // dlz[kQS][64] (delta / Z), zinv[kQS][64] (1 / Z) fp32
-constexpr uint32_t kSDoc = kSVec + 2048;       // query doc ids [8 warps][64] int32
+constexpr uint32_t kSdO = kSQ + kQS * 8192;    // dO stages [kQS]            8 KB each
+constexpr uint32_t kSG = kSdO + kQS * 8192;    // G [2] 128 keys x 64 q      16 KB each
+constexpr uint32_t kSStg = kSG + 2 * 16384;    // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
+constexpr uint32_t kSVec = kSStg + 32768;      // dlz[kQS][64] (delta / Z), zinv[kQS][64] (1 / Z) fp32
+constexpr uint32_t kSDoc = kSVec + kQS * 512;  // query doc ids [8 warps][64] int32
 constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
 constexpr uint32_t kSmemBytes = kSBar + 256;
+static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory per CTA");
 
 struct BwdParams {
   int B, H, T, Tpad;
@@ -106,13 +108,11 @@ struct BwdItem {
   int b, h, kt, n0, m_first, n_tiles;
 };
 
-// Work item idx: early key tiles (the most queries under a causal mask) first, then (b, h).
-// Query tiles [m_first, m_first + 64 n_tiles) can hold valid pairs for keys [n0, n0 + kBN).
-__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int idx) {
-  const int bh_total = p.B * p.H;
+// Work item (bh, kt): keys [n0, n0 + kBN) of head bh; query tiles [m_first, m_first + 64 n_tiles)
+// can hold valid pairs for them.
+__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int bh, int kt) {
   BwdItem it;
-  it.kt = idx / bh_total;
-  const int bh = idx % bh_total;
+  it.kt = kt;
   it.b = bh / p.H;
   it.h = bh % p.H;
   it.n0 = it.kt * kBN;
@@ -125,6 +125,40 @@ __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int idx) {
   return it;
 }
 
+// Schedule.  Items are numbered head-major, u = bh n_kv + kt, and the numbering is cut into
+// windows of 2 gridDim.x consecutive items (about 2 gridDim.x / n_kv heads).  Every item of a
+// head reads all of that head's Q, dO and 1/Z rows and reduce-adds into all of its fp32 dQ
+// accumulator rows, so while the CTAs work through one window only a few heads' rows are live
+// and they stay in L2 (ordering all key tile 0 items first keeps every head live at once, which
+// spills the accumulator to HBM).  Inside a window the items are sorted by key tile (under a
+// causal mask the early key tiles have the most query tiles) and dealt out as a snake: CTA c
+// takes window positions c and 2 gridDim.x - 1 - c, one long and one short item.
+// bwd_next: the item of this CTA's slot k, moving k past empty slots (the last window can be
+// short); false once the CTA has no items left.  Every role walks the same sequence.
+__device__ __forceinline__ bool bwd_next(const BwdParams& p, int& k, BwdItem& it) {
+  const int W = 2 * (int)gridDim.x;
+  for (;; ++k) {
+    const int a = (k >> 1) * W;  // first item of the window (n_items < 2^31)
+    if (a >= p.n_items) return false;
+    const int e = min(a + W, p.n_items);
+    int rem = (k & 1) ? W - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    if (rem >= e - a) continue;
+    // a = A n_kv + ra, e = E n_kv + re: the window holds key tile kt of heads
+    // A + [kt < ra] ..., (E - A) - [kt < ra] + [kt < re] of them
+    const int A = a / p.n_kv, ra = a - A * p.n_kv;
+    const int E = e / p.n_kv, re = e - E * p.n_kv;
+    for (int kt = 0; kt < p.n_kv; ++kt) {
+      const int c = (E - A) - (kt < ra ? 1 : 0) + (kt < re ? 1 : 0);
+      if (rem < c) {
+        it = bwd_item(p, A + (kt < ra ? 1 : 0) + rem, kt);
+        return true;
+      }
+      rem -= c;
+    }
+    return false;  // not reached: the per-key-tile counts add up to e - a
+  }
+}
+
 template <class Map, bool kHasDoc>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_bwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -133,20 +167,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
-  uint64_t* kv_full = bars + 0;    // [2] per item parity
-  uint64_t* kv_empty = bars + 2;   // [2]
-  uint64_t* q_full = bars + 4;     // [kQS] per query-tile stage
-  uint64_t* q_empty = bars + 8;    // [kQS]
-  uint64_t* sdp_full = bars + 12;  // [2] per query-tile parity
-  uint64_t* wg_full = bars + 14;   // [2]
-  uint64_t* mma_done = bars + 16;  // [2]
-  uint64_t* dq_full = bars + 18;   // [2]
-  uint64_t* dq_empty = bars + 20;  // [2]
-  uint64_t* acc_full = bars + 22;
-  uint64_t* acc_empty = bars + 23;
-  uint64_t* drain = bars + 24;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 26);
+  uint64_t* kv_full = bars + 0;              // [2] per item parity
+  uint64_t* kv_empty = bars + 2;             // [2]
+  uint64_t* q_full = bars + 4;               // [kQS] per query-tile stage
+  uint64_t* q_empty = bars + 4 + kQS;        // [kQS]
+  uint64_t* sdp_full = bars + 4 + 2 * kQS;   // [2] per query-tile parity
+  uint64_t* wg_full = bars + 6 + 2 * kQS;    // [2]
+  uint64_t* mma_done = bars + 8 + 2 * kQS;   // [2]
+  uint64_t* dq_full = bars + 10 + 2 * kQS;   // [2]
+  uint64_t* dq_empty = bars + 12 + 2 * kQS;  // [2]
+  uint64_t* acc_full = bars + 14 + 2 * kQS;
+  uint64_t* acc_empty = bars + 15 + 2 * kQS;
+  uint64_t* drain = bars + 16 + 2 * kQS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17 + 2 * kQS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18 + 2 * kQS);
+  static_assert((19 + 2 * kQS) * 8 <= 256, "barrier area");
   float* vdlz = reinterpret_cast<float*>(smem + kSVec);                // [kQS][64]
   float* vzinv = reinterpret_cast<float*>(smem + kSVec + kQS * 256);   // [kQS][64]
 
@@ -204,8 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         kv_issued = item_seq + 1;
         return true;
       };
-      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
-        const BwdItem it = bwd_item(p, idx);
+      int k = 0;
+      BwdItem it;
+      for (; ok && bwd_next(p, k, it); ++k, ++i) {
         const int64_t bh = (int64_t)it.b * p.H + it.h;
         if (kv_issued <= i) ok = load_kv(i, it);
         for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
@@ -219,7 +255,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
           bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
           // once this item's first query tile is on its way, fetch the next item's K and V
-          if (t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_kv(i + 1, bwd_item(p, idx + gridDim.x));
+          if (t == 0) {
+            int kn = k + 1;
+            BwdItem nit;
+            if (bwd_next(p, kn, nit)) ok = load_kv(i + 1, nit);
+          }
         }
       }
       if (!ok) {
@@ -273,8 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         have_prev = false;
         return true;
       };
-      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
-        const BwdItem it = bwd_item(p, idx);
+      int k = 0;
+      BwdItem it;
+      for (; ok && bwd_next(p, k, it); ++k, ++i) {
         ok = mbar_wait(&kv_full[i & 1], (i >> 1) & 1, wc, 22);
         const uint64_t dK = sdesc_sw128(smem_u32(smem + kSK + (i & 1) * 32768), 16, 1024);
         const uint64_t dV = sdesc_sw128(smem_u32(smem + kSV + (i & 1) * 32768), 16, 1024);
@@ -359,14 +400,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     int g = 0, i = 0;
     int prev_g = -1, prev_row = 0;
-    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
-      const BwdItem it = bwd_item(p, idx);
+    // per-item parameters (map, this key row's document id) come from global memory; those of
+    // the next item are requested before the current item's end-of-item work hides their latency
+    int k = 0;
+    BwdItem it_n;
+    bool have_n = bwd_next(p, k, it_n);
+    Map map_n{};
+    int doc_n = 0;
+    auto fetch = [&]() {
+      map_n = BwdMap<Map>::make(p, it_n.h);
+      if constexpr (kHasDoc) {
+        const int kr = it_n.n0 + jr;
+        doc_n = kr < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)kr * p.doc_s1] : -2;
+      }
+    };
+    if (have_n) fetch();
+    for (; ok && have_n; ++i) {
+      const BwdItem it = it_n;
+      const Map map = map_n;
+      const int doc_j = doc_n;
+      (void)doc_j;
       const int64_t bh = (int64_t)it.b * p.H + it.h;
       const int n0 = it.n0;
       const int kj = n0 + jr;
-      const Map map = BwdMap<Map>::make(p, it.h);
-      int doc_j = 0;
-      if constexpr (kHasDoc) doc_j = kj < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
       float g1 = 0.f, g2 = 0.f;
       for (int t = (wg - g) & 1; t < it.n_tiles && ok; t += 2) {
         const int gg = g + t;  // gg % 2 == wg
@@ -520,6 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&wg_full[sb]);
       }
       if (!ok) break;
+      ++k;
+      have_n = bwd_next(p, k, it_n);
+      if (have_n) fetch();
       // ---- end of the item: dK / dV rows (group 0 stores dV, group 1 stores dK), partials
       ok = __all_sync(0xffffffffu, mbar_wait(acc_full, i & 1, wc, 31));
       if (!ok) break;
