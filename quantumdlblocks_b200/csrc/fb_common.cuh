@@ -167,6 +167,7 @@ void record_cuda_error(cudaError_t e);
 // TMA tensor maps (fb_tmap.cu)
 bool get_encoder();
 bool tma_ok(const Tensor4& t);
-bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows);
+bool bh_mergeable(const Tensor4& t, int H);
+bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows, bool merge_bh);
 bool encode_rows_f32(CUtensorMap* m, float* base, int64_t rows);
 }  // namespace fb

@@ -121,6 +121,21 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Tile of a (B, H, T, D) tensor through a map built by encode_bhtd: 3-D (merged b*H + h) or 4-D.
+__device__ __forceinline__ void tma_load_bhtd(void* dst, const CUtensorMap* map, uint64_t* bar, bool map3, int x, int row,
+                                              int h, int b, int H) {
+  if (map3)
+    tma_load_3d(dst, map, bar, x, row, b * H + h);
+  else
+    tma_load_4d(dst, map, bar, x, row, h, b);
+}
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16)
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -1,36 +1,42 @@
-// fb_tc_bwd.cu -- flash-Born backward on the tcgen05 tensor cores (sm_100a), head dim 64.
+// fb_tc_bwd.cu -- flash-Born backward on the tcgen05 tensor cores (sm_100a), head dim 64 or 128.
 //
-// Three launches (all on the caller's stream):
-//   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
-//                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
-//   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
-//                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
-//                        tiles that can hold valid
-//                        pairs and accumulates dK, dV in TMEM; dQ partials are reduced into the
-//                        fp32 accumulator with TMA tensor reduce-add.  The query-tile pipeline
-//                        runs on across items (K, V double-buffered per item)
-//   3. bwd_post_kernel   dQ = accumulator -> input dtype
-//   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
-//                        sums and the main kernel's per-CTA partials
+// Four launches (all on the caller's stream):
+//   1. bwd_prep_kernel   (1 / Z_i, delta_i / Z_i) pairs with delta_i = sum_d dO_id O_id (per-head
+//                        rows padded to a multiple of 128), plus the closed-form sums of dscale /
+//                        dgamma
+//   2. tc_dkdv_kernel    persistent, key-major: one CTA per SM walks work items (batch, head,
+//                        128-key tile) in L2-resident windows of heads (bwd_next); each item walks
+//                        the 64-query tiles that can hold valid pairs and accumulates dK and dV in
+//                        TMEM (four products per tile)
+//   3. tc_dq_kernel      persistent, query-major: work items (batch, head, 128-query tile), heaviest
+//                        first; each item walks 64-key tiles, recomputes S and dP and accumulates
+//                        dQ = G K in TMEM (three products per tile), then stores dQ once
+//   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form sums
+//                        and the dK/dV kernel's per-warp partials
+// dQ is accumulated in TMEM by the CTA that owns its rows and written once: no fp32 atomics, so
+// every gradient is deterministic.  Splitting dQ off the key-major kernel frees the TMEM columns
+// its accumulators would take; the key-major kernel spends them on a third S^T/dP^T buffer (d=64)
+// or on the wider dK/dV accumulators (d=128).
 //
-// Per (key tile, query tile) the main kernel runs the five products the algorithm needs
-// (the reference's two kernels run six, flash_born.py:267-312 and :398-427):
-//   S^T  = K Q^T        M=128 keys, N=64 queries, K=64   A=K (smem K-major), B=Q (smem K-major)
-//   dP^T = V dO^T       same shape                        A=V, B=dO
-//   pointwise (thread = key row): a = relu(scale raw), p = a^2, W = p / Z_i,
-//     dP = (dP^T - delta_i) / Z_i, G = dL/draw = 2 a dP scale (masked; purified: 4u^3 dP gamma +
-//     2 eps_base b dP) -> W^T, G^T into TMEM (bf16, aliasing S^T / dP^T) and G into smem
-//   dV  += W^T dO       M=128, N=64, K=64 queries         A=W^T (TMEM), B=dO (smem MN-major)
-//   dK  += G^T Q        same                              A=G^T (TMEM), B=Q (smem MN-major)
-//   dQ_t = G K          M=64 queries, N=64, K=128 keys    A=G (smem MN-major), B=K (smem MN-major)
+// Per (key tile, query tile) the algorithm needs (flash_born.py:267-312 and :398-427):
+//   S^T  = K Q^T, dP^T = V dO^T                         (raw scores and dO.v, transposed)
+//   pointwise: a = relu(scale raw), p = a^2, W = p / Z_i, dP = (dP^T - delta_i) / Z_i,
+//              G = dL/draw = 2 a dP scale (masked; purified: 4u^3 dP gamma + 2 eps_base b dP)
+//   dV += W^T dO, dK += G^T Q                            (key-major kernel)
+//   S = Q K^T, dP = dO V^T, pointwise G, dQ += G K       (query-major kernel)
 //
-// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-9 two pointwise warpgroups
-// (key rows; group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two
-// groups' latency chains interleave).  Before each tile a group drains the dQ partial of its
-// previous tile (TMEM -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator).  S^T/dP^T/dQ are double-buffered in TMEM so
-// the products of query tile t+1 overlap the pointwise work of tile t.
+// Warps (352 threads, both main kernels): 0 TMA producers (copies issued by one thread complete
+// one after another, about 0.3 us each, so each operand stream has its own lane), 1 TMEM owner +
+// score-product issuer, 2-9 two pointwise warpgroups (group g takes the tiles t with t % 2 == g),
+// 10 gradient-product issuer.  One thread issues a tcgen05.mma at most every ~50 cycles, about
+// the execution time of an N = 64 product, so the two kinds of product are issued by two warps.
+// The score issuer runs up to kNB - 1 tiles ahead of the gradient issuer (kNB TMEM buffers), so
+// a group finds its next tile's scores ready when it finishes the current one.
 //
-// TMEM columns: S^T[0..1] 0/64, dP^T[0..1] 128/192, dV 256, dK 320, dQ[0..1] 384/448.
+// TMEM columns, key-major kernel:   d=64  S^T[3] 0/64/128, dP^T[3] 192/256/320, dV 384, dK 448
+//                                   d=128 S^T[2] 0/64, dP^T[2] 128/192, dV 256, dK 384
+//                 query-major kernel: S[3] 0/64/128, dP[3] 192/256/320, dQ 384 (d columns)
+// W^T / G^T (bf16) are written over the consumed S^T / dP^T columns, G over the consumed S columns.
 #include <cuda.h>
 
 #include <algorithm>
@@ -43,26 +49,9 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBN = 128;  // keys per CTA
-constexpr int kBM = 64;   // queries per step
-constexpr int kD = 64;
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;  // 11 warps
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTS = 0, kTdP = 128, kTdV = 256, kTdK = 320, kTdQ = 384;
-
-// shared memory carve-up (bytes from the 1024-aligned base)
-constexpr uint32_t kSK = 0;                    // K tiles [2 items] 128 x 64 bf16, 32 KB apart (K, V interleaved)
-constexpr uint32_t kSV = 16384;                // V tiles [2 items]
-constexpr int kQS = 4;                         // Q / dO / vector stages
-constexpr uint32_t kSQ = 65536;                // Q stages [kQS] 64 x 64     8 KB each
-constexpr uint32_t kSdO = kSQ + kQS * 8192;    // dO stages [kQS]            8 KB each
-constexpr uint32_t kSG = kSdO + kQS * 8192;    // G [2] 128 keys x 64 q      16 KB each
-constexpr uint32_t kSStg = kSG + 2 * 16384;    // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
-constexpr uint32_t kSVec = kSStg + 32768;      // dlz[kQS][64] (delta / Z), zinv[kQS][64] (1 / Z) fp32
-constexpr uint32_t kSDoc = kSVec + kQS * 512;  // query doc ids [8 warps][64] int32
-constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
-constexpr uint32_t kSmemBytes = kSBar + 256;
-static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory per CTA");
+constexpr int kRowPad = 128;  // per-head rows of the prep vectors are padded to this
 
 struct BwdParams {
   int B, H, T, Tpad;
@@ -78,11 +67,13 @@ struct BwdParams {
   int64_t dk_s0, dk_s1, dk_s2;
   __nv_bfloat16* dv;
   int64_t dv_s0, dv_s1, dv_s2;
-  const float* dlz;    // [BH][Tpad]  delta_i / Z_i
-  const float* zinv;   // [BH][Tpad]  1 / Z_i
-  float* dq_acc;       // [BH][Tpad][64]
+  __nv_bfloat16* dq;
+  int64_t dq_s0, dq_s1, dq_s2;
+  const float* zd;     // [BH][Tpad][2]  (1 / Z_i, delta_i / Z_i)
+  int map3;            // tensor maps address (b, h) as one merged dimension
   float* partials;     // [BH][n_kv][8 warps][2]
-  int n_kv, n_items;
+  int n_kv, n_items;   // key-major kernel: 128-key tiles per head, work items
+  int n_mt, n_qitems;  // query-major kernel: 128-query tiles per head, work items
   int* status;
 };
 
@@ -104,35 +95,61 @@ template <> struct BwdMap<PurifiedMapTC> {
   }
 };
 
+// =============================================================================================
+// Key-major kernel: dK, dV
+// =============================================================================================
+template <int D>
+struct KvCfg {
+  static constexpr int kBN = 128;  // keys per item (M of every product)
+  static constexpr int kBM = 64;   // queries per tile
+  static constexpr int kNB = D == 64 ? 3 : 2;    // S^T / dP^T TMEM buffers
+  static constexpr int kKVB = D == 64 ? 2 : 1;   // K / V item buffers (d=64: the next item's are prefetched)
+  static constexpr int kQS = D == 64 ? 8 : 4;    // Q / dO / vector stages
+  static constexpr uint32_t kKTile = kBN * D * 2;
+  static constexpr uint32_t kKHalf = kBN * 128;  // one 64-column half of a K or V tile
+  static constexpr uint32_t kQTile = kBM * D * 2;
+  static constexpr uint32_t kQHalf = kBM * 128;
+  static constexpr uint32_t kSK = 0;
+  static constexpr uint32_t kSV = kKVB * kKTile;
+  static constexpr uint32_t kSQ = 2 * kKVB * kKTile;
+  static constexpr uint32_t kSdO = kSQ + kQS * kQTile;
+  static constexpr uint32_t kSVec = kSdO + kQS * kQTile;  // [kQS][64 queries] (1/Z, delta/Z) fp32 pairs
+  static constexpr uint32_t kSDoc = kSVec + kQS * 512;     // query doc ids [8 warps][64] int32
+  static constexpr uint32_t kSBar = kSDoc + 8 * kBM * 4;
+  static constexpr uint32_t kSmem = kSBar + 512;
+  static constexpr uint32_t kTS = 0, kTdP = kNB * 64, kTdV = 2 * kNB * 64, kTdK = kTdV + D;
+  static_assert(kTdK + D <= kTmemCols, "TMEM columns");
+  static_assert(kSmem + 1024 <= 227 * 1024, "shared memory per CTA");
+  static_assert(4 + 4 * kQS + 3 * kNB + 4 <= 60, "barrier area");
+};
+
 struct BwdItem {
   int b, h, kt, n0, m_first, n_tiles;
 };
 
-// Work item (bh, kt): keys [n0, n0 + kBN) of head bh; query tiles [m_first, m_first + 64 n_tiles)
-// can hold valid pairs for them.
+// Work item (bh, kt): keys [n0, n0 + 128) of head bh; query tiles [m_first, m_first + 64 n_tiles)
+// can hold valid pairs for them (at least one: the key tile starts below T).
 __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int bh, int kt) {
   BwdItem it;
   it.kt = kt;
   it.b = bh / p.H;
   it.h = bh % p.H;
-  it.n0 = it.kt * kBN;
+  it.n0 = it.kt * 128;
   int lo = p.causal ? it.n0 : 0;
   int hi = p.T;
-  if (p.window > 0) hi = min(p.T, it.n0 + kBN - 1 + p.window);
-  lo = (lo / kBM) * kBM;
+  if (p.window > 0) hi = min(p.T, it.n0 + 128 - 1 + p.window);
+  lo = (lo / 64) * 64;
   it.m_first = lo;
-  it.n_tiles = hi > lo ? (hi - lo + kBM - 1) / kBM : 0;
+  it.n_tiles = hi > lo ? (hi - lo + 63) / 64 : 0;
   return it;
 }
 
 // Schedule.  Items are numbered head-major, u = bh n_kv + kt, and the numbering is cut into
 // windows of 2 gridDim.x consecutive items (about 2 gridDim.x / n_kv heads).  Every item of a
-// head reads all of that head's Q, dO and 1/Z rows and reduce-adds into all of its fp32 dQ
-// accumulator rows, so while the CTAs work through one window only a few heads' rows are live
-// and they stay in L2 (ordering all key tile 0 items first keeps every head live at once, which
-// spills the accumulator to HBM).  Inside a window the items are sorted by key tile (under a
-// causal mask the early key tiles have the most query tiles) and dealt out as a snake: CTA c
-// takes window positions c and 2 gridDim.x - 1 - c, one long and one short item.
+// head reads all of that head's Q, dO and 1/Z rows, so while the CTAs work through one window
+// only a few heads' rows are live and they stay in L2.  Inside a window the items are sorted by
+// key tile (under a causal mask the early key tiles have the most query tiles) and dealt out as
+// a snake: CTA c takes window positions c and 2 gridDim.x - 1 - c, one long and one short item.
 // bwd_next: the item of this CTA's slot k, moving k past empty slots (the last window can be
 // short); false once the CTA has no items left.  Every role walks the same sequence.
 __device__ __forceinline__ bool bwd_next(const BwdParams& p, int& k, BwdItem& it) {
@@ -159,53 +176,56 @@ __device__ __forceinline__ bool bwd_next(const BwdParams& p, int& k, BwdItem& it
   }
 }
 
-template <class Map, bool kHasDoc>
+template <int D, class Map, bool kHasDoc>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_bwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                  const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
-                  const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
+    tc_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+                   const BwdParams p) {
+  using C = KvCfg<D>;
+  constexpr int NB = C::kNB, KVB = C::kKVB, QS = C::kQS, BM = C::kBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
-  uint64_t* kv_full = bars + 0;              // [2] per item parity
-  uint64_t* kv_empty = bars + 2;             // [2]
-  uint64_t* q_full = bars + 4;               // [kQS] per query-tile stage
-  uint64_t* q_empty = bars + 4 + kQS;        // [kQS]
-  uint64_t* sdp_full = bars + 4 + 2 * kQS;   // [2] per query-tile parity
-  uint64_t* wg_full = bars + 6 + 2 * kQS;    // [2]
-  uint64_t* mma_done = bars + 8 + 2 * kQS;   // [2]
-  uint64_t* dq_full = bars + 10 + 2 * kQS;   // [2]
-  uint64_t* dq_empty = bars + 12 + 2 * kQS;  // [2]
-  uint64_t* acc_full = bars + 14 + 2 * kQS;
-  uint64_t* acc_empty = bars + 15 + 2 * kQS;
-  uint64_t* drain = bars + 16 + 2 * kQS;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17 + 2 * kQS);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 18 + 2 * kQS);
-  static_assert((19 + 2 * kQS) * 8 <= 256, "barrier area");
-  float* vdlz = reinterpret_cast<float*>(smem + kSVec);                // [kQS][64]
-  float* vzinv = reinterpret_cast<float*>(smem + kSVec + kQS * 256);   // [kQS][64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSBar);
+  uint64_t* kv_full = bars + 0;                // [2] per item
+  uint64_t* kv_empty = bars + 2;               // [2]
+  uint64_t* q_full = bars + 4;                 // [QS] per query-tile stage: Q
+  uint64_t* o_full = bars + 4 + QS;            // [QS] dO
+  uint64_t* vec_full = bars + 4 + 2 * QS;      // [QS] (1/Z, delta/Z) of the tile's queries
+  uint64_t* q_empty = bars + 4 + 3 * QS;       // [QS] the whole stage
+  uint64_t* sdp_full = bars + 4 + 4 * QS;      // [NB] per score buffer
+  uint64_t* wg_full = sdp_full + NB;           // [NB]
+  uint64_t* mma_done = wg_full + NB;           // [NB]
+  uint64_t* acc_full = mma_done + NB;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 60);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 61);
+  float* vzd = reinterpret_cast<float*>(smem + C::kSVec);  // [QS][64][2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx wc{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kQS; ++i) {
+    for (int i = 0; i < QS; ++i) {
       mbar_init(&q_full[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&vec_full[i], 1);
       mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < NB; ++i) {
       mbar_init(&sdp_full[i], 1);
       mbar_init(&wg_full[i], 128);
       mbar_init(&mma_done[i], 1);
-      mbar_init(&dq_full[i], 1);
-      mbar_init(&dq_empty[i], 128);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 256);
     mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -214,7 +234,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmV);
     prefetch_tensormap(&tmQ);
     prefetch_tensormap(&tmdO);
-    prefetch_tensormap(&tmDQ);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -226,16 +245,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (elect_one()) {
+    // ------------------------------------------------------------------ TMA producers
+    // Copies issued by one thread complete one after another, so the streams are split over
+    // lanes: lane 0 requests K / V of the items and Q of the query tiles, lane 1 dO, lane 2 the
+    // (1/Z, delta/Z) pairs; each walks the same tile sequence.
+    if (lane < 3) {
       bool ok = true;
-      int g = 0, i = 0, kv_issued = 0;
+      int g = 0, i = 0, kv_issued = 0, issued = 0;  // issued: this lane's query-tile copies requested
+      uint64_t* full = lane == 0 ? q_full : (lane == 1 ? o_full : vec_full);
       auto load_kv = [&](int item_seq, const BwdItem& it) -> bool {
-        const int kb = item_seq & 1;
-        if (item_seq >= 2 && !mbar_wait(&kv_empty[kb], ((item_seq >> 1) - 1) & 1, wc, 20)) return false;
-        mbar_arrive_expect_tx(&kv_full[kb], 2 * kBN * kD * 2);
-        tma_load_4d(smem + kSK + kb * 32768, &tmK, &kv_full[kb], 0, it.n0, it.h, it.b);
-        tma_load_4d(smem + kSV + kb * 32768, &tmV, &kv_full[kb], 0, it.n0, it.h, it.b);
+        const int kb = item_seq % KVB;
+        if (item_seq >= KVB && !mbar_wait(&kv_empty[kb], ((item_seq / KVB) - 1) & 1, wc, 20)) return false;
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * C::kKTile);
+#pragma unroll
+        for (int hf = 0; hf < D / 64; ++hf) {
+          tma_load_bhtd(smem + C::kSK + kb * C::kKTile + hf * C::kKHalf, &tmK, &kv_full[kb], p.map3, hf * 64, it.n0, it.h,
+                        it.b, p.H);
+          tma_load_bhtd(smem + C::kSV + kb * C::kKTile + hf * C::kKHalf, &tmV, &kv_full[kb], p.map3, hf * 64, it.n0, it.h,
+                        it.b, p.H);
+        }
         kv_issued = item_seq + 1;
         return true;
       };
@@ -243,19 +271,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       BwdItem it;
       for (; ok && bwd_next(p, k, it); ++k, ++i) {
         const int64_t bh = (int64_t)it.b * p.H + it.h;
-        if (kv_issued <= i) ok = load_kv(i, it);
+        if (lane == 0 && kv_issued <= i) ok = load_kv(i, it);
         for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
-          const int st = g % kQS;
-          if (g >= kQS) ok = mbar_wait(&q_empty[st], ((g / kQS) - 1) & 1, wc, 21);
+          const int st = g % QS;
+          if (g >= QS) ok = mbar_wait(&q_empty[st], ((g / QS) - 1) & 1, wc, 21);
           if (!ok) break;
-          const int m0 = it.m_first + t * kBM;
-          mbar_arrive_expect_tx(&q_full[st], 2 * kBM * kD * 2 + 2 * kBM * 4);
-          tma_load_4d(smem + kSQ + st * 8192, &tmQ, &q_full[st], 0, m0, it.h, it.b);
-          tma_load_4d(smem + kSdO + st * 8192, &tmdO, &q_full[st], 0, m0, it.h, it.b);
-          bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
-          bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &q_full[st]);
-          // once this item's first query tile is on its way, fetch the next item's K and V
-          if (t == 0) {
+          const int m0 = it.m_first + t * BM;
+          if (lane < 2) {
+            mbar_arrive_expect_tx(&full[st], C::kQTile);
+            const CUtensorMap* map = lane == 0 ? &tmQ : &tmdO;
+            uint8_t* dst = smem + (lane == 0 ? C::kSQ : C::kSdO) + st * C::kQTile;
+#pragma unroll
+            for (int hf = 0; hf < D / 64; ++hf)
+              tma_load_bhtd(dst + hf * C::kQHalf, map, &full[st], p.map3, hf * 64, m0, it.h, it.b, p.H);
+          } else {
+            mbar_arrive_expect_tx(&full[st], 2 * BM * 4);
+            bulk_load(vzd + st * 2 * BM, p.zd + (bh * p.Tpad + m0) * 2, 2 * BM * 4, &full[st]);
+          }
+          issued = g + 1;
+          // with two K/V buffers, the next item's K and V are requested once this item's first
+          // query tile is on its way
+          if (KVB == 2 && lane == 0 && t == 0) {
             int kn = k + 1;
             BwdItem nit;
             if (bwd_next(p, kn, nit)) ok = load_kv(i + 1, nit);
@@ -263,143 +299,115 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) {
-        for (int gg = max(0, g - kQS); gg < g; ++gg) mbar_wait_drain(&q_full[gg % kQS], (gg / kQS) & 1);
-        for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_wait_drain(&kv_full[ii & 1], (ii >> 1) & 1);
+        // abandoned: let this lane's copies already in flight land before the CTA exits
+        for (int gg = max(0, issued - QS); gg < issued; ++gg) mbar_wait_drain(&full[gg % QS], (gg / QS) & 1);
+        for (int ii = max(0, kv_issued - KVB); ii < kv_issued; ++ii)
+          mbar_wait_drain(&kv_full[ii % KVB], (ii / KVB) & 1);
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 10) {
+    // ------------------------------------------------------------------ MMA issuers
+    // warp 1: S^T, dP^T (score cursor); warp 10: dV, dK (gradient cursor)
     if (elect_one()) {
-      constexpr uint32_t idSdP = idesc_f16(1, 0, 0, kBM, kBN);  // N = 64 queries, M = 128 keys
-      constexpr uint32_t idAcc = idesc_f16(1, 0, 1, kD, kBN);   // A TMEM, B MN-major, N = 64
-      constexpr uint32_t idDQ = idesc_f16(1, 1, 1, kD, kBM);    // A, B MN-major, M = 64, N = 64
+      constexpr uint32_t idSdP = idesc_f16(1, 0, 0, BM, C::kBN);  // M = 128 keys, N = 64 queries
+      constexpr uint32_t idAcc = idesc_f16(1, 0, 1, D, C::kBN);   // A TMEM, B MN-major, N = D
       bool ok = true;
-      int g = 0, i = 0;
-      // the gradient products (dV, dK, dQ) of the previous query tile are issued after the next
-      // tile's S^T / dP^T, so the tensor core works while the pointwise groups run
-      bool have_prev = false;
-      int u_g = 0, u_i = 0;
-      bool u_first = false, u_last = false;
-      auto issue_grads = [&]() -> bool {
-        const int su = u_g & 1;
-        if (!mbar_wait(&wg_full[su], (u_g >> 1) & 1, wc, 25)) return false;
-        if (u_g >= 2 && !mbar_wait(&dq_empty[su], ((u_g - 2) >> 1) & 1, wc, 26)) return false;
-        if (u_first && u_i >= 1 && !mbar_wait(acc_empty, (u_i - 1) & 1, wc, 27)) return false;
+      // score cursor (S^T, dP^T) and gradient cursor (dV, dK) walk the same tile sequence; the
+      // score cursor runs up to NB - 1 tiles ahead
+      int s_k = 0, s_i = 0, s_t = 0, s_g = 0;
+      int u_k = 0, u_i = 0, u_t = 0, u_g = 0;
+      BwdItem s_it, u_it;
+      bool s_have = bwd_next(p, s_k, s_it);
+      bool u_have = bwd_next(p, u_k, u_it);
+      auto issue_sdp = [&]() -> bool {
+        const int b = s_g % NB;
+        const int qs = s_g % QS;
+        const int kb = s_i % KVB;
+        if (s_t == 0 && !mbar_wait(&kv_full[kb], (s_i / KVB) & 1, wc, 22)) return false;
+        if (!mbar_wait(&q_full[qs], (s_g / QS) & 1, wc, 23)) return false;
+        if (!mbar_wait(&o_full[qs], (s_g / QS) & 1, wc, 28)) return false;
+        // buffer b is free once the gradient products of tile s_g - NB have read W^T / G^T
+        if (s_g >= NB && !mbar_wait(&mma_done[b], ((s_g / NB) - 1) & 1, wc, 24)) return false;
         tc_fence_after();
-        const int qs = u_g % kQS;
-        // descriptors built once per operand; each K step adds its byte offset / 16 to the start
-        // address field (addresses stay below 256 KB, so the 14-bit field never carries)
-        const uint64_t dQmn = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 8192, 1024);
-        const uint64_t ddOmn = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 8192, 1024);
-        const uint64_t dG = sdesc_sw128(smem_u32(smem + kSG + su * 16384), 16384, 1024);
-        const uint64_t dKmn = sdesc_sw128(smem_u32(smem + kSK + (u_i & 1) * 32768), 16384, 1024);
+        const uint64_t dK = sdesc_sw128(smem_u32(smem + C::kSK + kb * C::kKTile), 16, 1024);
+        const uint64_t dV = sdesc_sw128(smem_u32(smem + C::kSV + kb * C::kKTile), 16, 1024);
+        const uint64_t dQ = sdesc_sw128(smem_u32(smem + C::kSQ + qs * C::kQTile), 16, 1024);
+        const uint64_t ddO = sdesc_sw128(smem_u32(smem + C::kSdO + qs * C::kQTile), 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns, 2048 B of dO
-          mma_ts(tmem + kTdV, tmem + kTS + su * kBM + kk * 8, ddOmn + kk * 128, idAcc, (u_first && kk == 0) ? 0u : 1u);
-#pragma unroll
-        for (int kk = 0; kk < kBM / 16; ++kk)
-          mma_ts(tmem + kTdK, tmem + kTdP + su * kBM + kk * 8, dQmn + kk * 128, idAcc, (u_first && kk == 0) ? 0u : 1u);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)  // 16 keys per step: 2048 B of G and of K
-          mma_ss(tmem + kTdQ + su * kD, dG + kk * 128, dKmn + kk * 128, idDQ, kk > 0);
-        mma_commit(&q_empty[qs]);
-        mma_commit(&dq_full[su]);
-        mma_commit(&mma_done[su]);
-        if (u_last) {
-          mma_commit(acc_full);
-          mma_commit(&kv_empty[u_i & 1]);
+        for (int kk = 0; kk < D / 16; ++kk) {  // 16 head-dim elements per step (32 B along a row)
+          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
+          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + C::kTS + b * 64, dK + ok_, dQ + oq_, idSdP, kk > 0);
         }
-        have_prev = false;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
+          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + C::kTdP + b * 64, dV + ok_, ddO + oq_, idSdP, kk > 0);
+        }
+        mma_commit(&sdp_full[b]);
+        // K and V feed only the score products: the item's buffer is free after its last one
+        if (s_t == s_it.n_tiles - 1) mma_commit(&kv_empty[kb]);
+        ++s_g;
+        if (++s_t == s_it.n_tiles) {
+          s_t = 0;
+          ++s_i;
+          ++s_k;
+          s_have = bwd_next(p, s_k, s_it);
+        }
         return true;
       };
-      int k = 0;
-      BwdItem it;
-      for (; ok && bwd_next(p, k, it); ++k, ++i) {
-        ok = mbar_wait(&kv_full[i & 1], (i >> 1) & 1, wc, 22);
-        const uint64_t dK = sdesc_sw128(smem_u32(smem + kSK + (i & 1) * 32768), 16, 1024);
-        const uint64_t dV = sdesc_sw128(smem_u32(smem + kSV + (i & 1) * 32768), 16, 1024);
-        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
-          const int sb = g & 1;
-          const int qs = g % kQS;
-          ok = mbar_wait(&q_full[qs], (g / kQS) & 1, wc, 23);
-          if (ok && g >= 2) ok = mbar_wait(&mma_done[sb], ((g - 2) >> 1) & 1, wc, 24);
-          if (!ok) break;
-          tc_fence_after();
-          const uint64_t dQ = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 16, 1024);
-          const uint64_t ddO = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 16, 1024);
+      auto issue_grads = [&]() -> bool {
+        const int b = u_g % NB;
+        const int qs = u_g % QS;
+        if (!mbar_wait(&wg_full[b], (u_g / NB) & 1, wc, 25)) return false;
+        if (u_t == 0 && u_i >= 1 && !mbar_wait(acc_empty, (u_i - 1) & 1, wc, 27)) return false;
+        tc_fence_after();
+        // MN-major Q / dO (N = head dim): 64-column blocks kQHalf apart, a K step of 16 queries
+        // is 16 rows = 2048 B
+        const uint64_t dQmn = sdesc_sw128(smem_u32(smem + C::kSQ + qs * C::kQTile), C::kQHalf, 1024);
+        const uint64_t ddOmn = sdesc_sw128(smem_u32(smem + C::kSdO + qs * C::kQTile), C::kQHalf, 1024);
+        const uint32_t acc = (u_t == 0) ? 0u : 1u;
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements per step: 32 B along the row
-            mma_ss(tmem + kTS + sb * kBM, dK + kk * 2, dQ + kk * 2, idSdP, kk > 0);
+        for (int kk = 0; kk < BM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns
+          mma_ts(tmem + C::kTdV, tmem + C::kTS + b * 64 + kk * 8, ddOmn + kk * 128, idAcc, (kk == 0) ? acc : 1u);
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_ss(tmem + kTdP + sb * kBM, dV + kk * 2, ddO + kk * 2, idSdP, kk > 0);
-          mma_commit(&sdp_full[sb]);
-          if (have_prev) ok = issue_grads();
-          if (!ok) break;
-          have_prev = true;
-          u_g = g;
-          u_i = i;
-          u_first = t == 0;
-          u_last = t == it.n_tiles - 1;
+        for (int kk = 0; kk < BM / 16; ++kk)
+          mma_ts(tmem + C::kTdK, tmem + C::kTdP + b * 64 + kk * 8, dQmn + kk * 128, idAcc, (kk == 0) ? acc : 1u);
+        mma_commit(&q_empty[qs]);
+        mma_commit(&mma_done[b]);
+        if (u_t == u_it.n_tiles - 1) mma_commit(acc_full);
+        ++u_g;
+        if (++u_t == u_it.n_tiles) {
+          u_t = 0;
+          ++u_i;
+          ++u_k;
+          u_have = bwd_next(p, u_k, u_it);
         }
+        return true;
+      };
+      const int role = warp == 1 ? 0 : 1;
+      if (role == 0) {
+        while (ok && s_have) ok = issue_sdp();
+      } else {
+        while (ok && u_have) ok = issue_grads();
       }
-      if (ok && have_prev) ok = issue_grads();
-      if (!ok) {
-        mma_commit(drain);
-        mbar_wait_drain(drain, 0);
+      if (!ok) {  // wait for this thread's products in flight before TMEM is released
+        mma_commit(drain + role);
+        mbar_wait_drain(drain + role, 0);
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------------ pointwise (key rows)
+    // ------------------------------------------------------------------ pointwise (key rows), warps 2-9
     const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;
     const int jr = lg * 32 + lane;  // key row within the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
-    int* docq = reinterpret_cast<int*>(smem + kSDoc) + (wg * 4 + lg) * kBM;
-    uint8_t* g_row0 = smem + kSG + jr * 128;
-    uint8_t* stg = smem + kSStg + lg * 8192 + wg * 4096;  // this warp's dQ staging (two 16 x 32 boxes)
-    const bool leader = elect_one();
+    int* docq = reinterpret_cast<int*>(smem + C::kSDoc) + (wg * 4 + lg) * BM;
     bool ok = true;
-    // dQ partial of global query tile u (TMEM buffer wg; an M=64 accumulator keeps rows
-    // 16lg..16lg+15 in lanes 0..15 of this warp's quadrant) -> swizzled staging -> TMA
-    // reduce-add into the fp32 accumulator at row grow
-    auto drain_dq = [&](int u, int grow) -> bool {
-      if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[wg], (u >> 1) & 1, wc, 29))) return false;
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld32(lane_addr + kTdQ + wg * kD, r0);
-      tmem_ld32(lane_addr + kTdQ + wg * kD + 32, r1);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&dq_empty[wg]);
-      if (leader) bulk_wait_read<0>();  // the previous reduce from this staging buffer has read it
-      __syncwarp();
-      if (lane < 16) {
-        uint8_t* row0 = stg + lane * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4*>(row0 + ((c ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(r0[4 * c]), __uint_as_float(r0[4 * c + 1]), __uint_as_float(r0[4 * c + 2]),
-                          __uint_as_float(r0[4 * c + 3]));
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<float4*>(row0 + 2048 + ((c ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(r1[4 * c]), __uint_as_float(r1[4 * c + 1]), __uint_as_float(r1[4 * c + 2]),
-                          __uint_as_float(r1[4 * c + 3]));
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (leader) {
-        tma_reduce_add_2d(&tmDQ, stg, 0, grow + 16 * lg);
-        tma_reduce_add_2d(&tmDQ, stg + 2048, 32, grow + 16 * lg);
-        bulk_commit();
-      }
-      return true;
-    };
     int g = 0, i = 0;
-    int prev_g = -1, prev_row = 0;
     // per-item parameters (map, this key row's document id) come from global memory; those of
     // the next item are requested before the current item's end-of-item work hides their latency
     int k = 0;
@@ -426,44 +434,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       float g1 = 0.f, g2 = 0.f;
       for (int t = (wg - g) & 1; t < it.n_tiles && ok; t += 2) {
         const int gg = g + t;  // gg % 2 == wg
-        const int sb = wg;
-        const int m0 = it.m_first + t * kBM;
-        if (prev_g >= 0) {
-          ok = drain_dq(prev_g, prev_row);
-          if (!ok) break;
-        }
-        prev_g = gg;
-        prev_row = (int)(bh * p.Tpad + m0);
+        const int b = gg % NB;
+        const int qs = gg % QS;
+        const int m0 = it.m_first + t * BM;
         if constexpr (kHasDoc) {
 #pragma unroll
-          for (int u = 0; u < kBM / 32; ++u) {
+          for (int u = 0; u < BM / 32; ++u) {
             const int qi = m0 + u * 32 + lane;
             docq[u * 32 + lane] = qi < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
           }
           __syncwarp();
         }
-        ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[sb], (gg >> 1) & 1, wc, 30));
+        ok = __all_sync(0xffffffffu, mbar_wait(&vec_full[qs], (gg / QS) & 1, wc, 32));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[b], (gg / NB) & 1, wc, 30));
         if (!ok) break;
         tc_fence_after();
-        const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
-                          (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
-                          (n0 + kBN <= p.T);
+        const bool full = !kHasDoc && (!p.causal || m0 >= n0 + C::kBN - 1) &&
+                          (p.window <= 0 || (m0 + BM - 1) - n0 < p.window) && (m0 + BM <= p.T) &&
+                          (n0 + C::kBN <= p.T);
         // causal diagonal tiles (m0 = n0 or n0 + 64, all keys < T): for query chunk c of warp lg,
         // with d = 32 c + (m0 - n0) - 32 lg, query column e is valid iff e + d >= lane
-        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 + kBN <= p.T;
-        const float* dl = vdlz + (gg % kQS) * kBM;
-        const float* zi = vzinv + (gg % kQS) * kBM;
-        uint8_t* g_row = g_row0 + sb * 16384;
-        const uint32_t s_col = lane_addr + kTS + sb * kBM, p_col = lane_addr + kTdP + sb * kBM;
-        // one 16-query sub-chunk of a fully valid tile: W, G -> TMEM (over consumed columns), G -> smem
+        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 + C::kBN <= p.T;
+        const float4* zd4 = reinterpret_cast<const float4*>(vzd + qs * 2 * BM);  // (z, d) of two queries each
+        const uint32_t s_col = lane_addr + C::kTS + b * 64, p_col = lane_addr + C::kTdP + b * 64;
+        // one 16-query sub-chunk of a fully valid tile: W^T, G^T -> TMEM over consumed columns
         auto sub16 = [&](int sc, const uint32_t (&rs)[16], const uint32_t (&rd)[16]) {
           float zc[16], dc[16];
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            const float4 z4 = reinterpret_cast<const float4*>(zi + sc * 16)[v4];
-            const float4 d4 = reinterpret_cast<const float4*>(dl + sc * 16)[v4];
-            zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
-            dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+          for (int v2 = 0; v2 < 8; ++v2) {
+            const float4 f = zd4[sc * 8 + v2];
+            zc[2 * v2] = f.x; dc[2 * v2] = f.y; zc[2 * v2 + 1] = f.z; dc[2 * v2 + 1] = f.w;
           }
           uint32_t wpk[8], gpk[8];
 #pragma unroll
@@ -480,8 +480,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st8(s_col + sc * 8, wpk);
           tmem_st8(p_col + sc * 8, gpk);
-          *reinterpret_cast<uint4*>(g_row + (((2 * sc) ^ (jr & 7)) << 4)) = make_uint4(gpk[0], gpk[1], gpk[2], gpk[3]);
-          *reinterpret_cast<uint4*>(g_row + (((2 * sc + 1) ^ (jr & 7)) << 4)) = make_uint4(gpk[4], gpk[5], gpk[6], gpk[7]);
         };
         if (full) {
           // software pipeline: the TMEM loads of sub-chunk s+1 are in flight while s is computed
@@ -490,12 +488,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(p_col, dA);
           tmem_wait_ld();
 #pragma unroll
-          for (int sc = 0; sc < kBM / 16; sc += 2) {
+          for (int sc = 0; sc < BM / 16; sc += 2) {
             tmem_ld16(s_col + (sc + 1) * 16, sB);
             tmem_ld16(p_col + (sc + 1) * 16, dB);
             sub16(sc, sA, dA);
             tmem_wait_ld();
-            if (sc + 2 < kBM / 16) {
+            if (sc + 2 < BM / 16) {
               tmem_ld16(s_col + (sc + 2) * 16, sA);
               tmem_ld16(p_col + (sc + 2) * 16, dA);
             }
@@ -504,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 #pragma unroll 1
-        for (int c = 0; c < (full ? 0 : kBM / 32); ++c) {
+        for (int c = 0; c < (full ? 0 : BM / 32); ++c) {
           uint32_t wpk[16], gpk[16];
           const int d = 32 * c + (m0 - n0) - 32 * lg;
           if (diag && d <= -32) {  // every key of this warp is after every query of the chunk
@@ -512,15 +510,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 16; ++e) wpk[e] = gpk[e] = 0u;
           } else {
             uint32_t rs[32], rd[32];
-            tmem_ld32(lane_addr + kTS + sb * kBM + c * 32, rs);
-            tmem_ld32(lane_addr + kTdP + sb * kBM + c * 32, rd);
+            tmem_ld32(s_col + c * 32, rs);
+            tmem_ld32(p_col + c * 32, rd);
             float zc[32], dc[32];  // per-query 1/Z and delta/Z of these 32 columns (shared, broadcast)
 #pragma unroll
-            for (int v4 = 0; v4 < 8; ++v4) {
-              const float4 z4 = reinterpret_cast<const float4*>(zi + c * 32)[v4];
-              const float4 d4 = reinterpret_cast<const float4*>(dl + c * 32)[v4];
-              zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
-              dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+            for (int v2 = 0; v2 < 16; ++v2) {
+              const float4 f = zd4[c * 16 + v2];
+              zc[2 * v2] = f.x; dc[2 * v2] = f.y; zc[2 * v2 + 1] = f.z; dc[2 * v2 + 1] = f.w;
             }
             tmem_wait_ld();
             if (diag && d >= 31) {
@@ -560,20 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          tmem_st16(lane_addr + kTS + sb * kBM + c * 16, wpk);   // W^T over the consumed S^T columns
-          tmem_st16(lane_addr + kTdP + sb * kBM + c * 16, gpk);  // G^T over the consumed dP^T columns
-          // G (MN-major A operand of dQ): key row jr holds 64 queries = 128 B, 16-byte chunks swizzled
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int chunk = c * 4 + x;
-            *reinterpret_cast<uint4*>(g_row + ((chunk ^ (jr & 7)) << 4)) =
-                make_uint4(gpk[4 * x], gpk[4 * x + 1], gpk[4 * x + 2], gpk[4 * x + 3]);
-          }
+          tmem_st16(s_col + c * 16, wpk);  // W^T over the consumed S^T columns
+          tmem_st16(p_col + c * 16, gpk);  // G^T over the consumed dP^T columns
         }
         tmem_wait_st();
-        fence_proxy_async_smem();  // G written by the generic proxy, read by the tensor core
         tc_fence_before();
-        mbar_arrive(&wg_full[sb]);
+        mbar_arrive(&wg_full[b]);
       }
       if (!ok) break;
       ++k;
@@ -584,28 +572,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK), r0);
-        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK) + 32, r1);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(acc_empty);
-        if (kj < p.T) {
-          __nv_bfloat16* dst = wg == 0 ? p.dv + (int64_t)it.b * p.dv_s0 + (int64_t)it.h * p.dv_s1 + (int64_t)kj * p.dv_s2
-                                       : p.dk + (int64_t)it.b * p.dk_s0 + (int64_t)it.h * p.dk_s1 + (int64_t)kj * p.dk_s2;
-          uint4* d4 = reinterpret_cast<uint4*>(dst);
+        const uint32_t acc_col = lane_addr + (wg == 0 ? C::kTdV : C::kTdK);
+        __nv_bfloat16* dst = wg == 0 ? p.dv + (int64_t)it.b * p.dv_s0 + (int64_t)it.h * p.dv_s1 + (int64_t)kj * p.dv_s2
+                                     : p.dk + (int64_t)it.b * p.dk_s0 + (int64_t)it.h * p.dk_s1 + (int64_t)kj * p.dk_s2;
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            d4[v4] = make_uint4(pack2<true>(__uint_as_float(r0[8 * v4]), __uint_as_float(r0[8 * v4 + 1])),
-                                pack2<true>(__uint_as_float(r0[8 * v4 + 2]), __uint_as_float(r0[8 * v4 + 3])),
-                                pack2<true>(__uint_as_float(r0[8 * v4 + 4]), __uint_as_float(r0[8 * v4 + 5])),
-                                pack2<true>(__uint_as_float(r0[8 * v4 + 6]), __uint_as_float(r0[8 * v4 + 7])));
+        for (int hf = 0; hf < D / 64; ++hf) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(acc_col + hf * 64, r0);
+          tmem_ld32(acc_col + hf * 64 + 32, r1);
+          tmem_wait_ld();
+          if (hf == D / 64 - 1) {
+            tc_fence_before();
+            mbar_arrive(acc_empty);
+          }
+          if (kj < p.T) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + hf * 64);
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4)
-            d4[4 + v4] = make_uint4(pack2<true>(__uint_as_float(r1[8 * v4]), __uint_as_float(r1[8 * v4 + 1])),
-                                    pack2<true>(__uint_as_float(r1[8 * v4 + 2]), __uint_as_float(r1[8 * v4 + 3])),
-                                    pack2<true>(__uint_as_float(r1[8 * v4 + 4]), __uint_as_float(r1[8 * v4 + 5])),
-                                    pack2<true>(__uint_as_float(r1[8 * v4 + 6]), __uint_as_float(r1[8 * v4 + 7])));
+            for (int v4 = 0; v4 < 4; ++v4)
+              d4[v4] = make_uint4(pack2<true>(__uint_as_float(r0[8 * v4]), __uint_as_float(r0[8 * v4 + 1])),
+                                  pack2<true>(__uint_as_float(r0[8 * v4 + 2]), __uint_as_float(r0[8 * v4 + 3])),
+                                  pack2<true>(__uint_as_float(r0[8 * v4 + 4]), __uint_as_float(r0[8 * v4 + 5])),
+                                  pack2<true>(__uint_as_float(r0[8 * v4 + 6]), __uint_as_float(r0[8 * v4 + 7])));
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4)
+              d4[4 + v4] = make_uint4(pack2<true>(__uint_as_float(r1[8 * v4]), __uint_as_float(r1[8 * v4 + 1])),
+                                      pack2<true>(__uint_as_float(r1[8 * v4 + 2]), __uint_as_float(r1[8 * v4 + 3])),
+                                      pack2<true>(__uint_as_float(r1[8 * v4 + 4]), __uint_as_float(r1[8 * v4 + 5])),
+                                      pack2<true>(__uint_as_float(r1[8 * v4 + 6]), __uint_as_float(r1[8 * v4 + 7])));
+          }
         }
       }
 #pragma unroll
@@ -620,9 +614,394 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       g += it.n_tiles;
     }
-    if (ok && prev_g >= 0) ok = drain_dq(prev_g, prev_row);
-    if (leader) bulk_wait<0>();  // every reduce has finished reading shared memory
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// =============================================================================================
+// Query-major kernel: dQ
+// =============================================================================================
+template <int D>
+struct DqCfg {
+  static constexpr int kBM = 128;  // queries per item (M of every product)
+  static constexpr int kBN = 64;   // keys per tile
+  static constexpr int kNB = 3;    // S / dP TMEM buffers
+  static constexpr int kQB = D == 64 ? 2 : 1;   // Q / dO item buffers (d=64: the next item's are prefetched)
+  static constexpr int kKS = D == 64 ? 8 : 5;   // K stages (held until dQ += G K of the tile)
+  static constexpr int kVS = D == 64 ? 6 : 4;   // V stages (held until dP of the tile)
+  static constexpr uint32_t kQTile = kBM * D * 2;
+  static constexpr uint32_t kQHalf = kBM * 128;
+  static constexpr uint32_t kKTile = kBN * D * 2;
+  static constexpr uint32_t kKHalf = kBN * 128;
+  static constexpr uint32_t kSQ = 0;
+  static constexpr uint32_t kSdO = kQB * kQTile;
+  static constexpr uint32_t kSK = 2 * kQB * kQTile;
+  static constexpr uint32_t kSV = kSK + kKS * kKTile;
+  static constexpr uint32_t kSDoc = kSV + kVS * kKTile;  // key doc ids [8 warps][64] int32
+  static constexpr uint32_t kSBar = kSDoc + 8 * kBN * 4;
+  static constexpr uint32_t kSmem = kSBar + 512;
+  static constexpr uint32_t kTS = 0, kTdP = kNB * 64, kTdQ = 2 * kNB * 64;
+  static_assert(kTdQ + D <= kTmemCols, "TMEM columns");
+  static_assert(kSmem + 1024 <= 227 * 1024, "shared memory per CTA");
+  static_assert(4 + 2 * kKS + 2 * kVS + 3 * kNB + 4 <= 60, "barrier area");
+};
+
+struct QItem {
+  int b, h, m0, n_first, n_count;
+};
+
+// Work item idx of the query-major kernel: latest query tiles (the most keys under a causal
+// mask) first, then (b, h).  Keys [n_first, n_first + 64 n_count) can be valid for its rows.
+__device__ __forceinline__ QItem q_item(const BwdParams& p, int idx) {
+  const int bh_total = p.B * p.H;
+  const int mt = p.n_mt - 1 - idx / bh_total;
+  const int bh = idx % bh_total;
+  QItem it;
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  it.m0 = mt * 128;
+  int lo = 0, hi = p.T;
+  if (p.causal) hi = min(p.T, it.m0 + 128);
+  if (p.window > 0) lo = max(0, it.m0 - p.window + 1);
+  lo = (lo / 64) * 64;
+  it.n_first = lo;
+  it.n_count = hi > lo ? (hi - lo + 63) / 64 : 0;
+  return it;
+}
+
+template <int D, class Map, bool kHasDoc>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+                 const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const BwdParams p) {
+  using C = DqCfg<D>;
+  constexpr int NB = C::kNB, QB = C::kQB, KS = C::kKS, VS = C::kVS, BN = C::kBN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSBar);
+  uint64_t* q_full = bars + 0;           // [2] per item
+  uint64_t* q_empty = bars + 2;          // [2]
+  uint64_t* k_full = bars + 4;           // [KS]
+  uint64_t* k_empty = k_full + KS;       // [KS]
+  uint64_t* v_full = k_empty + KS;       // [VS]
+  uint64_t* v_empty = v_full + VS;       // [VS]
+  uint64_t* s_full = v_empty + VS;       // [NB] per score buffer
+  uint64_t* g_full = s_full + NB;        // [NB]
+  uint64_t* mma_done = g_full + NB;      // [NB]
+  uint64_t* dq_full = mma_done + NB;
+  uint64_t* dq_empty = dq_full + 1;
+  uint64_t* drain = dq_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 60);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 61);
+  int* docs_all = reinterpret_cast<int*>(smem + C::kSDoc);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtx wc{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < KS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&g_full[i], 128);
+      mbar_init(&mma_done[i], 1);
+    }
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 256);
+    mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmdO);
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producers
+    // lane 0 requests Q / dO of the items and K of the key tiles, lane 1 V (copies issued by one
+    // thread complete one after another)
+    if (lane < 2) {
+      bool ok = true;
+      int g = 0, i = 0, q_issued = 0, issued = 0;  // issued: K (lane 0) or V (lane 1) tiles requested
+      const int NS = lane == 0 ? KS : VS;
+      uint64_t* full = lane == 0 ? k_full : v_full;
+      uint64_t* empty = lane == 0 ? k_empty : v_empty;
+      const CUtensorMap* map = lane == 0 ? &tmK : &tmV;
+      uint8_t* ring = smem + (lane == 0 ? C::kSK : C::kSV);
+      auto load_q = [&](int item_seq, const QItem& it) -> bool {
+        const int qb = item_seq % QB;
+        if (item_seq >= QB && !mbar_wait(&q_empty[qb], ((item_seq / QB) - 1) & 1, wc, 40)) return false;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * C::kQTile);
+#pragma unroll
+        for (int hf = 0; hf < D / 64; ++hf) {
+          tma_load_bhtd(smem + C::kSQ + qb * C::kQTile + hf * C::kQHalf, &tmQ, &q_full[qb], p.map3, hf * 64, it.m0, it.h,
+                        it.b, p.H);
+          tma_load_bhtd(smem + C::kSdO + qb * C::kQTile + hf * C::kQHalf, &tmdO, &q_full[qb], p.map3, hf * 64, it.m0,
+                        it.h, it.b, p.H);
+        }
+        q_issued = item_seq + 1;
+        return true;
+      };
+      for (int idx = blockIdx.x; idx < p.n_qitems && ok; idx += gridDim.x, ++i) {
+        const QItem it = q_item(p, idx);
+        if (lane == 0 && q_issued <= i) ok = load_q(i, it);
+        for (int t = 0; t < it.n_count && ok; ++t, ++g) {
+          const int st = g % NS;
+          const int n0 = it.n_first + t * BN;
+          // a K stage is free once dQ += G K of its tile has completed, a V stage once dP has
+          if (g >= NS) ok = mbar_wait(&empty[st], ((g / NS) - 1) & 1, wc, 41 + lane);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[st], C::kKTile);
+#pragma unroll
+          for (int hf = 0; hf < D / 64; ++hf)
+            tma_load_bhtd(ring + st * C::kKTile + hf * C::kKHalf, map, &full[st], p.map3, hf * 64, n0, it.h, it.b, p.H);
+          issued = g + 1;
+          // with two Q / dO buffers, the next item's are requested once this item's first key
+          // tile is on its way
+          if (QB == 2 && lane == 0 && t == 0 && idx + (int)gridDim.x < p.n_qitems)
+            ok = load_q(i + 1, q_item(p, idx + gridDim.x));
+        }
+      }
+      if (!ok) {
+        // abandoned: let this lane's copies already in flight land before the CTA exits
+        for (int gg = max(0, issued - NS); gg < issued; ++gg) mbar_wait_drain(&full[gg % NS], (gg / NS) & 1);
+        for (int qq = max(0, q_issued - QB); qq < q_issued; ++qq) mbar_wait_drain(&q_full[qq % QB], (qq / QB) & 1);
+      }
+    }
     __syncwarp();
+  } else if (warp == 1 || warp == 10) {
+    // ------------------------------------------------------------------ MMA issuers
+    // warp 1: S, dP (score cursor); warp 10: dQ += G K (gradient cursor)
+    if (elect_one()) {
+      constexpr uint32_t idS = idesc_f16(1, 0, 0, BN, C::kBM);  // M = 128 queries, N = 64 keys
+      constexpr uint32_t idQ = idesc_f16(1, 0, 1, D, C::kBM);   // A TMEM (G), B MN-major (K), N = D
+      bool ok = true;
+      int s_idx = blockIdx.x, s_i = 0, s_t = 0, s_g = 0;
+      int u_idx = blockIdx.x, u_i = 0, u_t = 0, u_g = 0;
+      QItem s_it{}, u_it{};
+      bool s_have = s_idx < p.n_qitems, u_have = u_idx < p.n_qitems;
+      if (s_have) s_it = q_item(p, s_idx);
+      if (u_have) u_it = q_item(p, u_idx);
+      auto issue_sdp = [&]() -> bool {
+        const int b = s_g % NB;
+        const int qb = s_i % QB;
+        if (s_t == 0 && !mbar_wait(&q_full[qb], (s_i / QB) & 1, wc, 43)) return false;
+        if (!mbar_wait(&k_full[s_g % KS], (s_g / KS) & 1, wc, 44)) return false;
+        if (!mbar_wait(&v_full[s_g % VS], (s_g / VS) & 1, wc, 45)) return false;
+        // buffer b is free once dQ += G K of tile s_g - NB has read G
+        if (s_g >= NB && !mbar_wait(&mma_done[b], ((s_g / NB) - 1) & 1, wc, 46)) return false;
+        tc_fence_after();
+        const uint64_t dQ = sdesc_sw128(smem_u32(smem + C::kSQ + qb * C::kQTile), 16, 1024);
+        const uint64_t ddO = sdesc_sw128(smem_u32(smem + C::kSdO + qb * C::kQTile), 16, 1024);
+        const uint64_t dK = sdesc_sw128(smem_u32(smem + C::kSK + (s_g % KS) * C::kKTile), 16, 1024);
+        const uint64_t dV = sdesc_sw128(smem_u32(smem + C::kSV + (s_g % VS) * C::kKTile), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
+          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + C::kTS + b * 64, dQ + oq_, dK + ok_, idS, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
+          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
+          mma_ss(tmem + C::kTdP + b * 64, ddO + oq_, dV + ok_, idS, kk > 0);
+        }
+        mma_commit(&s_full[b]);
+        mma_commit(&v_empty[s_g % VS]);
+        if (s_t == s_it.n_count - 1) mma_commit(&q_empty[qb]);  // Q and dO feed only the score products
+        ++s_g;
+        if (++s_t == s_it.n_count) {
+          s_t = 0;
+          ++s_i;
+          s_idx += gridDim.x;
+          s_have = s_idx < p.n_qitems;
+          if (s_have) s_it = q_item(p, s_idx);
+        }
+        return true;
+      };
+      auto issue_dq = [&]() -> bool {
+        const int b = u_g % NB;
+        if (!mbar_wait(&g_full[b], (u_g / NB) & 1, wc, 47)) return false;
+        if (u_t == 0 && u_i >= 1 && !mbar_wait(dq_empty, (u_i - 1) & 1, wc, 48)) return false;
+        tc_fence_after();
+        // K as the MN-major B operand (N = head dim): 64-column blocks kKHalf apart, a K step of
+        // 16 keys is 16 rows = 2048 B
+        const uint64_t dKmn = sdesc_sw128(smem_u32(smem + C::kSK + (u_g % KS) * C::kKTile), C::kKHalf, 1024);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per step: 8 packed TMEM columns of G
+          mma_ts(tmem + C::kTdQ, tmem + C::kTS + b * 64 + kk * 8, dKmn + kk * 128, idQ, (u_t == 0 && kk == 0) ? 0u : 1u);
+        mma_commit(&k_empty[u_g % KS]);
+        mma_commit(&mma_done[b]);
+        if (u_t == u_it.n_count - 1) mma_commit(dq_full);
+        ++u_g;
+        if (++u_t == u_it.n_count) {
+          u_t = 0;
+          ++u_i;
+          u_idx += gridDim.x;
+          u_have = u_idx < p.n_qitems;
+          if (u_have) u_it = q_item(p, u_idx);
+        }
+        return true;
+      };
+      const int role = warp == 1 ? 0 : 1;
+      if (role == 0) {
+        while (ok && s_have) ok = issue_sdp();
+      } else {
+        while (ok && u_have) ok = issue_dq();
+      }
+      if (!ok) {  // wait for this thread's products in flight before TMEM is released
+        mma_commit(drain + role);
+        mbar_wait_drain(drain + role, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ pointwise (query rows), warps 2-9
+    const int wg = (warp - 2) >> 2;
+    const int lg = warp & 3;
+    const int row = lg * 32 + lane;  // query row within the item == TMEM lane
+    int* docs_k = docs_all + (wg * 4 + lg) * BN;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    bool ok = true;
+    int g = 0, i = 0;
+    // per-item, per-row parameters from global memory; the next item's are requested before the
+    // current item's epilogue
+    QItem it_n{};
+    Map map_n{};
+    int doc_n = 0;
+    float zinv_n = 0.f, dlz_n = 0.f;
+    auto fetch = [&](int idx) {
+      it_n = q_item(p, idx);
+      map_n = BwdMap<Map>::make(p, it_n.h);
+      const int q = it_n.m0 + row;
+      const int64_t vrow = ((int64_t)it_n.b * p.H + it_n.h) * p.Tpad + q;  // q < Tpad (a multiple of 128)
+      const float2 zd = reinterpret_cast<const float2*>(p.zd)[vrow];
+      zinv_n = zd.x;
+      dlz_n = zd.y;
+      if constexpr (kHasDoc) doc_n = q < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)q * p.doc_s1] : -1;
+    };
+    if (blockIdx.x < p.n_qitems) fetch(blockIdx.x);
+    for (int idx = blockIdx.x; idx < p.n_qitems && ok; idx += gridDim.x, ++i) {
+      const QItem it = it_n;
+      const Map map = map_n;
+      const int doc_i = doc_n;
+      const float zinv = zinv_n, dlz = dlz_n;
+      (void)doc_i;
+      const int qi = it.m0 + row;
+      float unused1 = 0.f, unused2 = 0.f;
+      for (int t = (wg - g) & 1; t < it.n_count && ok; t += 2) {
+        const int gg = g + t;  // gg % 2 == wg
+        const int b = gg % NB;
+        const int n0 = it.n_first + t * BN;
+        if constexpr (kHasDoc) {
+#pragma unroll
+          for (int u = 0; u < BN / 32; ++u) {
+            const int kj = n0 + u * 32 + lane;
+            docs_k[u * 32 + lane] = kj < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)kj * p.doc_s1] : -2;
+          }
+          __syncwarp();
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (gg / NB) & 1, wc, 50));
+        if (!ok) break;
+        tc_fence_after();
+        const bool full = !kHasDoc && (!p.causal || n0 + BN - 1 <= it.m0) &&
+                          (p.window <= 0 || (it.m0 + C::kBM - 1) - n0 < p.window) && (n0 + BN <= p.T);
+        const uint32_t s_col = lane_addr + C::kTS + b * 64, p_col = lane_addr + C::kTdP + b * 64;
+        // two 32-key chunks; chunk c writes G (16 packed columns) over S columns [16c, 16c + 16),
+        // which chunk 0 has already read
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t rs[32], rd[32];
+          tmem_ld32(s_col + c * 32, rs);
+          tmem_ld32(p_col + c * 32, rd);
+          tmem_wait_ld();
+          uint32_t gpk[16];
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float gv[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u)
+                gv[u] = map.grad(__uint_as_float(rs[e + u]), true, fmaf(__uint_as_float(rd[e + u]), zinv, -dlz),
+                                 unused1, unused2);
+              gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+            }
+          } else {
+            const int kbase = n0 + c * 32;
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float gv[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                int doc_j = 0;
+                if constexpr (kHasDoc) doc_j = docs_k[c * 32 + e + u];
+                const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
+                gv[u] = map.grad(__uint_as_float(rs[e + u]), valid, fmaf(__uint_as_float(rd[e + u]), zinv, -dlz),
+                                 unused1, unused2);
+              }
+              gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+            }
+          }
+          tmem_st16(s_col + c * 16, gpk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&g_full[b]);
+      }
+      if (!ok) break;
+      if (idx + (int)gridDim.x < p.n_qitems) fetch(idx + gridDim.x);
+      // ---- epilogue of the item: dQ rows (group wg stores head-dim columns [wg D/2, (wg+1) D/2))
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, i & 1, wc, 51));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[D / 2];
+#pragma unroll
+      for (int cc = 0; cc < D / 64; ++cc)
+        tmem_ld32(lane_addr + C::kTdQ + wg * (D / 2) + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(r + cc * 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      if (qi < p.T) {
+        uint4* dst = reinterpret_cast<uint4*>(p.dq + (int64_t)it.b * p.dq_s0 + (int64_t)it.h * p.dq_s1 +
+                                              (int64_t)qi * p.dq_s2 + wg * (D / 2));
+#pragma unroll
+        for (int v4 = 0; v4 < D / 16; ++v4)
+          dst[v4] = make_uint4(pack2<true>(__uint_as_float(r[8 * v4]), __uint_as_float(r[8 * v4 + 1])),
+                               pack2<true>(__uint_as_float(r[8 * v4 + 2]), __uint_as_float(r[8 * v4 + 3])),
+                               pack2<true>(__uint_as_float(r[8 * v4 + 4]), __uint_as_float(r[8 * v4 + 5])),
+                               pack2<true>(__uint_as_float(r[8 * v4 + 6]), __uint_as_float(r[8 * v4 + 7])));
+      }
+      g += it.n_count;
+    }
   }
 
   tc_fence_before();
@@ -634,7 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Pre / post passes
+// Pre pass and parameter sums
 // ---------------------------------------------------------------------------------------------
 struct AuxParams {
   int B, H, T, Tpad, D;
@@ -648,11 +1027,7 @@ struct AuxParams {
   const __nv_bfloat16* dout;
   int64_t do_s0, do_s1, do_s2, do_s3;
   const float* z;
-  float* dlz;
-  float* zinv;
-  float* dq_acc;
-  __nv_bfloat16* dq;
-  int64_t dq_s0, dq_s1, dq_s2;
+  float* zd;  // [BH][Tpad][2]  (1 / Z_i, delta_i / Z_i)
   const float* partials;
   int n_kv;
   float* dscale;
@@ -660,14 +1035,16 @@ struct AuxParams {
   int scale_per_head, tau_per_head;
 };
 
-// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id),
-// a zeroed dQ accumulator chunk, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
-// dscale / d gamma).  Eight lanes share a row (8 elements = 16 bytes of bf16 each), so a warp
-// reads four 128-byte rows per load instruction.
+// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id;
+// rows at or beyond T get zeros), and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
+// dscale / d gamma).  Eight lanes share a row (D / 8 elements each, 16-byte loads), so a warp
+// reads four rows per step.
+template <int D>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
+  constexpr int kPer = D / 8;  // elements per lane
   const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int sub = lane >> 3, part = lane & 7;  // row within the group of 4, 8-element slice
+  const int sub = lane >> 3, part = lane & 7;  // row within the group of 4, slice of the row
   const int64_t bh = (int64_t)b * a.H + h;
   __shared__ float csum_w[8];
   float csum = 0.f;
@@ -677,41 +1054,39 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
     const int64_t row = bh * a.Tpad + i;
     float s = 0.f;
     if (i < a.T) {
-      const int d0 = part * 8;
+      const int d0 = part * kPer;
       const __nv_bfloat16* dop = a.dout + (int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 + d0;
-      const uint4 dv = *reinterpret_cast<const uint4*>(dop);
-      float o[8];
       const int64_t oo = (int64_t)b * a.o_s0 + (int64_t)h * a.o_s1 + (int64_t)i * a.o_s2 + d0;
-      if (a.out_f32) {
-        const float4 x = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[0];
-        const float4 y = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[1];
-        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
-      } else {
-        const uint4 ov = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out) + oo);
-        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
 #pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          o[2 * x] = sm100::bf16_lo(ow[x]);
-          o[2 * x + 1] = sm100::bf16_hi(ow[x]);
+      for (int v = 0; v < kPer / 8; ++v) {
+        const uint4 dv = reinterpret_cast<const uint4*>(dop)[v];
+        float o[8];
+        if (a.out_f32) {
+          const float4 x = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[2 * v];
+          const float4 y = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[2 * v + 1];
+          o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
+        } else {
+          const uint4 ov = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out) + oo)[v];
+          const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            o[2 * x] = sm100::bf16_lo(ow[x]);
+            o[2 * x + 1] = sm100::bf16_hi(ow[x]);
+          }
         }
-      }
-      const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
 #pragma unroll
-      for (int x = 0; x < 4; ++x) s += o[2 * x] * sm100::bf16_lo(dw[x]) + o[2 * x + 1] * sm100::bf16_hi(dw[x]);
+        for (int x = 0; x < 4; ++x) s += o[2 * x] * sm100::bf16_lo(dw[x]) + o[2 * x + 1] * sm100::bf16_hi(dw[x]);
+      }
     }
 #pragma unroll
     for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (part == 0) {
       const float zi = i < a.T ? 1.f / a.z[bh * a.T + i] : 0.f;
-      a.dlz[row] = s * zi;
-      a.zinv[row] = zi;
+      reinterpret_cast<float2*>(a.zd)[row] = make_float2(zi, s * zi);
       csum += a.eps * s * zi;
     }
   }
-  // zero this chunk's 64 accumulator rows (64 x 64 fp32 = 16 KB, one float4 per thread x 4)
-  float4* acc = reinterpret_cast<float4*>(a.dq_acc + (bh * a.Tpad + chunk * 64) * a.D);
-#pragma unroll
-  for (int x = 0; x < 4; ++x) acc[x * 256 + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, off);
   if (lane == 0) csum_w[warp] = csum;
@@ -723,33 +1098,12 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
   }
 }
 
-// dQ accumulator -> bf16 (one thread per 8 elements)
-__global__ void __launch_bounds__(256) bwd_post_kernel(const AuxParams a) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int per_row = a.D / 8;
-  const int64_t rows = (int64_t)a.B * a.H * a.T;
-  if (idx >= rows * per_row) return;
-  const int c8 = (int)(idx % per_row);
-  const int64_t r = idx / per_row;
-  const int i = (int)(r % a.T);
-  const int64_t bh = r / a.T;
-  const int h = (int)(bh % a.H), b = (int)(bh / a.H);
-  const float4* src = reinterpret_cast<const float4*>(a.dq_acc + ((bh * a.Tpad + i) * a.D + c8 * 8));
-  const float4 x = src[0], y = src[1];
-  uint4 o;
-  o.x = sm100::pack2<true>(x.x, x.y);
-  o.y = sm100::pack2<true>(x.z, x.w);
-  o.z = sm100::pack2<true>(y.x, y.y);
-  o.w = sm100::pack2<true>(y.z, y.w);
-  *reinterpret_cast<uint4*>(a.dq + (int64_t)b * a.dq_s0 + (int64_t)h * a.dq_s1 + (int64_t)i * a.dq_s2 + c8 * 8) = o;
-}
-
 // Fixed-order sums into dscale / dtau (deterministic; replaces atomics, flash_born.py:319-322):
 //   plain     dscale_h = (2 / scale_h) sum_{b,i} eps delta_i / Z_i
 //   purified  dgamma_h = (4 / gamma_h) (sum_{b,i} eps delta_i / Z_i - sum eps_base b^2 dP),
-//             dtau_h   = sum -4 u^3 dP gamma        (the last two from the main kernel's partials)
-// One block per head: each thread sums a fixed strided subset, then a fixed-shape tree; block 0
-// also folds the heads together for shared (scalar) parameters after a second pass.
+//             dtau_h   = sum -4 u^3 dP gamma        (the last two from the dK/dV kernel's partials)
+// One block per head: each thread sums a fixed strided subset, then a fixed-shape tree; the
+// per-head terms are folded together for shared (scalar) parameters by a second kernel.
 __global__ void __launch_bounds__(256) bwd_param_kernel(const AuxParams a, float* head_terms) {
   const int h = blockIdx.x;
   const int nc = a.Tpad / 64;
@@ -801,20 +1155,20 @@ __global__ void bwd_param_shared_kernel(const AuxParams a, const float* head_ter
 }
 
 struct WsLayout {
-  size_t dlz, zinv, dq_acc, partials, prep_part, head_terms, total;
+  size_t zd, partials, prep_part, head_terms, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+int row_pad(int T) { return (T + kRowPad - 1) / kRowPad * kRowPad; }
+
 WsLayout ws_layout(const Problem& p) {
-  const int Tpad = (p.T + kBM - 1) / kBM * kBM;
+  const int Tpad = row_pad(p.T);
   const size_t BH = (size_t)p.B * p.H;
-  const int n_kv = (p.T + kBN - 1) / kBN;
+  const int n_kv = (p.T + 127) / 128;
   WsLayout w;
-  w.dlz = 0;
-  w.zinv = align256(w.dlz + BH * Tpad * 4);
-  w.dq_acc = align256(w.zinv + BH * Tpad * 4);
-  w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
+  w.zd = 0;
+  w.partials = align256(w.zd + BH * Tpad * 8);
   w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
   w.head_terms = align256(w.prep_part + BH * (Tpad / 64) * 4);
   w.total = align256(w.head_terms + (size_t)p.H * 2 * 4);
@@ -840,24 +1194,51 @@ bool rows16(const Tensor4& t) {  // 16-byte vector row stores of bf16 rows
   return true;
 }
 
-template <class Map, bool kHasDoc>
-int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp, const CUtensorMap& mk, const CUtensorMap& mv,
-                const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mdq) {
-  auto kernel = tc_bwd_kernel<Map, kHasDoc>;
-  const uint32_t smem = kSmemBytes + 1024;
+template <int D, class Map, bool kHasDoc>
+int launch_kv(cudaStream_t s, const BwdParams& bp, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mq,
+              const CUtensorMap& mdo) {
+  auto kernel = tc_dkdv_kernel<D, Map, kHasDoc>;
+  const uint32_t smem = KvCfg<D>::kSmem + 1024;  // + alignment slack
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
-  dim3 grid(std::min(bp.n_items, bwd_num_sms()));
-  kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, mdq, bp);
+  kernel<<<std::min(bp.n_items, bwd_num_sms()), kThreads, smem, s>>>(mk, mv, mq, mdo, bp);
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   return FB_OK;
 }
 
+template <int D, class Map, bool kHasDoc>
+int launch_dq(cudaStream_t s, const BwdParams& bp, const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mk,
+              const CUtensorMap& mv) {
+  auto kernel = tc_dq_kernel<D, Map, kHasDoc>;
+  const uint32_t smem = DqCfg<D>::kSmem + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  kernel<<<std::min(bp.n_qitems, bwd_num_sms()), kThreads, smem, s>>>(mq, mdo, mk, mv, bp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  return FB_OK;
+}
+
+template <int D, class Map>
+int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp) {
+  CUtensorMap kk, kv, kq, kdo, qq, qdo, qk, qv;
+  const bool m3 = bp.map3 != 0;
+  // key-major kernel: K / V boxes of 128 rows, Q / dO of 64; query-major: the other way round
+  if (!encode_bhtd(&kk, pr.k, pr.B, pr.H, pr.T, D, 128, m3) || !encode_bhtd(&kv, pr.v, pr.B, pr.H, pr.T, D, 128, m3) ||
+      !encode_bhtd(&kq, pr.q, pr.B, pr.H, pr.T, D, 64, m3) || !encode_bhtd(&kdo, pr.dout, pr.B, pr.H, pr.T, D, 64, m3) ||
+      !encode_bhtd(&qq, pr.q, pr.B, pr.H, pr.T, D, 128, m3) || !encode_bhtd(&qdo, pr.dout, pr.B, pr.H, pr.T, D, 128, m3) ||
+      !encode_bhtd(&qk, pr.k, pr.B, pr.H, pr.T, D, 64, m3) || !encode_bhtd(&qv, pr.v, pr.B, pr.H, pr.T, D, 64, m3))
+    return FB_ERR_ALIGN;
+  int rc = pr.doc ? launch_kv<D, Map, true>(s, bp, kk, kv, kq, kdo) : launch_kv<D, Map, false>(s, bp, kk, kv, kq, kdo);
+  if (rc != FB_OK) return rc;
+  return pr.doc ? launch_dq<D, Map, true>(s, bp, qq, qdo, qk, qv) : launch_dq<D, Map, false>(s, bp, qq, qdo, qk, qv);
+}
+
 }  // namespace
 
 bool tc_bwd_supported(const Problem& p) {
-  if (p.dtype != FB_BF16 || p.D != kD) return false;
+  if (p.dtype != FB_BF16 || (p.D != 64 && p.D != 128)) return false;
   if (p.out_dtype != FB_BF16 && p.out_dtype != FB_F32) return false;
   if (!tma_ok(p.q) || !tma_ok(p.k) || !tma_ok(p.v) || !tma_ok(p.dout)) return false;
   if (!rows16(p.dq) || !rows16(p.dk) || !rows16(p.dv)) return false;
@@ -873,14 +1254,11 @@ size_t tc_bwd_workspace(const Problem& p) { return ws_layout(p).total; }
 
 int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (!get_encoder()) return FB_ERR_NO_DEVICE;
-  CUtensorMap mk, mv, mq, mdo;
-  if (!encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D, kBN) || !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D, kBN) ||
-      !encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D, kBM) || !encode_bhtd(&mdo, pr.dout, pr.B, pr.H, pr.T, pr.D, kBM))
-    return FB_ERR_ALIGN;
   const WsLayout w = ws_layout(pr);
   char* ws = static_cast<char*>(pr.ws);
-  const int Tpad = (pr.T + kBM - 1) / kBM * kBM;
-  const int n_kv = (pr.T + kBN - 1) / kBN;
+  const int Tpad = row_pad(pr.T);
+  const int n_kv = (pr.T + 127) / 128;
+  const int n_mt = (pr.T + 127) / 128;
 
   AuxParams a{};
   a.B = pr.B; a.H = pr.H; a.T = pr.T; a.Tpad = Tpad; a.D = pr.D;
@@ -894,11 +1272,7 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   a.dout = static_cast<const __nv_bfloat16*>(pr.dout.ptr);
   a.do_s0 = pr.dout.s[0]; a.do_s1 = pr.dout.s[1]; a.do_s2 = pr.dout.s[2]; a.do_s3 = pr.dout.s[3];
   a.z = pr.z;
-  a.dlz = reinterpret_cast<float*>(ws + w.dlz);
-  a.zinv = reinterpret_cast<float*>(ws + w.zinv);
-  a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
-  a.dq = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dq.ptr));
-  a.dq_s0 = pr.dq.s[0]; a.dq_s1 = pr.dq.s[1]; a.dq_s2 = pr.dq.s[2];
+  a.zd = reinterpret_cast<float*>(ws + w.zd);
   a.partials = reinterpret_cast<float*>(ws + w.partials);
   a.n_kv = n_kv;
   a.dscale = pr.dscale;
@@ -916,27 +1290,30 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   bp.dk_s0 = pr.dk.s[0]; bp.dk_s1 = pr.dk.s[1]; bp.dk_s2 = pr.dk.s[2];
   bp.dv = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dv.ptr));
   bp.dv_s0 = pr.dv.s[0]; bp.dv_s1 = pr.dv.s[1]; bp.dv_s2 = pr.dv.s[2];
-  bp.dlz = a.dlz; bp.zinv = a.zinv; bp.dq_acc = a.dq_acc;
+  bp.dq = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dq.ptr));
+  bp.dq_s0 = pr.dq.s[0]; bp.dq_s1 = pr.dq.s[1]; bp.dq_s2 = pr.dq.s[2];
+  bp.zd = a.zd;
   bp.partials = reinterpret_cast<float*>(ws + w.partials);
   bp.n_kv = n_kv;
   bp.n_items = n_kv * pr.B * pr.H;
+  bp.n_mt = n_mt;
+  bp.n_qitems = n_mt * pr.B * pr.H;
   bp.status = pr.status;
+  bp.map3 = bh_mergeable(pr.q, pr.H) && bh_mergeable(pr.k, pr.H) && bh_mergeable(pr.v, pr.H) &&
+            bh_mergeable(pr.dout, pr.H);
 
-  CUtensorMap mdq;
-  if (!encode_rows_f32(&mdq, a.dq_acc, (int64_t)pr.B * pr.H * Tpad)) return FB_ERR_ALIGN;
-  bwd_prep_kernel<<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
+  if (pr.D == 64)
+    bwd_prep_kernel<64><<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
+  else
+    bwd_prep_kernel<128><<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   int rc;
-  if (pr.purified)
-    rc = pr.doc ? launch_main<PurifiedMapTC, true>(pr, s, bp, mk, mv, mq, mdo, mdq)
-                : launch_main<PurifiedMapTC, false>(pr, s, bp, mk, mv, mq, mdo, mdq);
+  if (pr.D == 64)
+    rc = pr.purified ? launch_main<64, PurifiedMapTC>(pr, s, bp) : launch_main<64, PlainMapNoParam>(pr, s, bp);
   else
-    rc = pr.doc ? launch_main<PlainMapNoParam, true>(pr, s, bp, mk, mv, mq, mdo, mdq)
-                : launch_main<PlainMapNoParam, false>(pr, s, bp, mk, mv, mq, mdo, mdq);
+    rc = pr.purified ? launch_main<128, PurifiedMapTC>(pr, s, bp) : launch_main<128, PlainMapNoParam>(pr, s, bp);
   if (rc != FB_OK) return rc;
-  const int64_t post_threads = (int64_t)pr.B * pr.H * pr.T * (pr.D / 8);
-  bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
   bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
   int n = 4;

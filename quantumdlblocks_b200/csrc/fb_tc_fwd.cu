@@ -7,22 +7,25 @@
 // TMEM double buffers and the mbarrier phases run on from one item into the next and the
 // per-item set-up latency is hidden.  Warp-specialised pipeline (320 threads):
 //
-//   warp 0      TMA producer: Q of an item (double-buffered, the next item's Q is fetched
-//               while the current one runs), K_j and V_j through rings of kStages stages with
-//               separate full and empty barriers: a K stage is released when S_j completes, a V
-//               stage when O += P_j V_j does, and V runs one tile behind K in the issue order, so
-//               K_{j+kStages} is requested about one tile earlier than a shared K/V stage allows
-//   warp 1      TMEM owner + MMA issuer (one elected lane):
+//   warp 0      TMA producers: copies issued by one thread complete one after another (about
+//               0.3 us each, whatever their size), so lane 0 requests Q of an item (double-
+//               buffered, the next item's Q is fetched while the current one runs) and K_j, and
+//               lane 1 requests V_j, through rings of kStages stages with separate full and empty
+//               barriers: a K stage is released when S_j completes, a V stage when O += P_j V_j does
+//   warp 1      TMEM owner + S issuer (one elected lane):
 //                 S_g = Q K_g^T      tcgen05.mma kind::f16, A = Q (smem, K-major),
 //                                    B = K_g (smem, K-major), D = S[g%2] in TMEM (fp32)
+//   warp 10     O += P V issuer (one elected lane; one thread issues a tcgen05.mma at most every
+//               ~50 cycles, longer than an N = 80 product takes, so the two products get a warp each):
 //                 O  += P_g V_g      A = P[g%2] (TMEM, bf16 packed), B = V_g (smem, MN-major),
 //                                    D = O in TMEM (fp32); the first tile of an item overwrites O.
 //                                    For d=64 the same MMA also produces the row sums: N = 80,
 //                                    and the B columns 64..79 are a ones tile in shared memory
 //                                    (reached through the descriptor's leading-byte offset), so
 //                                    TMEM columns O[64..80) accumulate Z = P 1.
-//               S_{g+1} is issued before O += P_g V_g so the tensor core works while the
-//               pointwise warps turn S_g into P_g.
+//               S_{g+2} waits until the pointwise group has read S_g (p_full), so S runs up to
+//               two tiles ahead of O += P V and the tensor core works while the pointwise warps
+//               turn S_g into P_g.
 //   warps 2-9   two pointwise ("Born") warpgroups; group w handles the tiles with g % 2 == w
 //               (TMEM buffers S[w], P[w]); thread r of a group owns TMEM lane r = query row r.
 //               tcgen05.ld S row -> a = relu(scale s) (masked), p = a^2, P = bf16(p) ->
@@ -52,7 +55,7 @@ using namespace sm100;
 
 constexpr int kBM = 128;       // queries per item (one M=128 MMA)
 constexpr int kBN = 128;       // keys per tile
-constexpr int kThreads = 320;  // 10 warps
+constexpr int kThreads = 352;  // 11 warps
 constexpr uint32_t kTmemCols = 512;
 
 template <int D>
@@ -81,6 +84,7 @@ struct FwdCfg {
 
 struct FwdParams {
   int B, H, T;
+  int map3;           // tensor maps address (b, h) as one merged dimension
   int n_mt, n_items;  // query tiles per head, work items
   int causal, window;
   float eps, eps_base;
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_empty = bars + 11 + 4 * S;
   uint64_t* z_bar = bars + 12 + 4 * S;
   uint64_t* drain = bars + 13 + 4 * S;
-  static_assert(14 + 4 * S <= 48, "barrier area");
+  static_assert(15 + 4 * S <= 48, "barrier area");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 48);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 49);
   int* docs_all = reinterpret_cast<int*>(smem + Cfg::kDocOff);
@@ -178,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(o_empty, 256);
     mbar_init(z_bar, 256);
     mbar_init(drain, 1);
+    mbar_init(drain + 1, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -201,110 +206,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (elect_one()) {
+    // ------------------------------------------------------------------ TMA producers
+    // Copies issued by one thread complete one after another, so the streams are split over
+    // lanes: lane 0 requests Q and K, lane 1 requests V; each walks the same tile sequence.
+    if (lane < 2) {
       bool ok = true;
-      int g = 0, i = 0, q_issued = 0, v_issued = 0;
-      int vb = 0, vh = 0, vn0 = 0;  // coordinates of the V tile still to be requested (tile v_issued)
+      int g = 0, i = 0, q_issued = 0, issued = 0;  // issued: K (lane 0) or V (lane 1) tiles requested
+      uint64_t* full = lane == 0 ? k_full : v_full;
+      uint64_t* empty = lane == 0 ? k_empty : v_empty;
+      const CUtensorMap* map = lane == 0 ? &tmK : &tmV;
+      uint8_t* ring = smem + (lane == 0 ? Cfg::kKOff : Cfg::kVOff);
       auto load_q = [&](int item_seq, const Item& it) -> bool {
         const int qb = item_seq & 1;
         if (item_seq >= 2 && !mbar_wait(&q_empty[qb], ((item_seq >> 1) - 1) & 1, wc, 1)) return false;
         mbar_arrive_expect_tx(&q_full[qb], Cfg::kTileBytes);
 #pragma unroll
         for (int hf = 0; hf < Cfg::kHalves; ++hf)
-          tma_load_4d(smem + Cfg::kQOff + qb * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmQ, &q_full[qb], hf * 64,
-                      it.m0, it.h, it.b);
+          tma_load_bhtd(smem + Cfg::kQOff + qb * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmQ, &q_full[qb], p.map3,
+                        hf * 64, it.m0, it.h, it.b, p.H);
         q_issued = item_seq + 1;
-        return true;
-      };
-      // V of tile v_issued, once O += P V of the tile kStages earlier has released its stage
-      auto load_v = [&]() -> bool {
-        const int vs = v_issued % S;
-        if (v_issued >= S && !mbar_wait(&v_empty[vs], ((v_issued / S) - 1) & 1, wc, 12)) return false;
-        mbar_arrive_expect_tx(&v_full[vs], Cfg::kTileBytes);
-#pragma unroll
-        for (int hf = 0; hf < Cfg::kHalves; ++hf)
-          tma_load_4d(smem + Cfg::kVOff + vs * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmV, &v_full[vs], hf * 64,
-                      vn0, vh, vb);
-        ++v_issued;
         return true;
       };
       for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
         const Item it = item_at(p, idx);
-        if (q_issued <= i) ok = load_q(i, it);
+        if (lane == 0 && q_issued <= i) ok = load_q(i, it);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
           const int st = g % S;
-          if (g >= S) ok = mbar_wait(&k_empty[st], ((g / S) - 1) & 1, wc, 2);
+          // stage st is free once S_{g-S} (K) or O += P_{g-S} V_{g-S} (V) has completed
+          if (g >= S) ok = mbar_wait(&empty[st], ((g / S) - 1) & 1, wc, 2 + 10 * lane);
           if (!ok) break;
           const int n0 = it.n_first + t * kBN;
-          mbar_arrive_expect_tx(&k_full[st], Cfg::kTileBytes);
+          mbar_arrive_expect_tx(&full[st], Cfg::kTileBytes);
 #pragma unroll
           for (int hf = 0; hf < Cfg::kHalves; ++hf)
-            tma_load_4d(smem + Cfg::kKOff + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, &tmK, &k_full[st], hf * 64,
-                        n0, it.h, it.b);
-          if (v_issued < g) ok = load_v();  // V of the previous tile
-          if (!ok) break;
-          vb = it.b;
-          vh = it.h;
-          vn0 = n0;
+            tma_load_bhtd(ring + st * Cfg::kTileBytes + hf * Cfg::kHalfBytes, map, &full[st], p.map3, hf * 64, n0, it.h,
+                          it.b, p.H);
+          issued = g + 1;
           // once the first K of this item is on its way, fetch the next item's Q
-          if (t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_q(i + 1, item_at(p, idx + gridDim.x));
+          if (lane == 0 && t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_q(i + 1, item_at(p, idx + gridDim.x));
         }
       }
-      if (ok && v_issued < g) ok = load_v();  // V of the last tile
       if (!ok) {
-        // abandoned: let the copies already in flight land before the CTA exits (g K tiles and
-        // v_issued V tiles were requested)
-        for (int gg = max(0, g - S); gg < g; ++gg) mbar_wait_drain(&k_full[gg % S], (gg / S) & 1);
-        for (int gg = max(0, v_issued - S); gg < v_issued; ++gg) mbar_wait_drain(&v_full[gg % S], (gg / S) & 1);
+        // abandoned: let this lane's copies already in flight land before the CTA exits
+        for (int gg = max(0, issued - S); gg < issued; ++gg) mbar_wait_drain(&full[gg % S], (gg / S) & 1);
         for (int qq = max(0, q_issued - 2); qq < q_issued; ++qq) mbar_wait_drain(&q_full[qq & 1], (qq >> 1) & 1);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------------ S issuer
     if (elect_one()) {
       constexpr uint32_t idS = idesc_f16(1, 0, 0, kBN, kBM);  // S: A K-major, B K-major, N = 128
-      // O (and for d=64 Z): A TMEM, B MN-major, N = D (+16 ones columns)
-      constexpr uint32_t idO = idesc_f16(1, 0, 1, Cfg::kTcZ ? D + 16 : D, kBM);
-      const uint32_t ones_base = smem_u32(smem + Cfg::kOnesOff);
       bool ok = true;
       int g = 0, i = 0;
-      // pending O += P V of the previous tile
-      bool have_prev = false;
-      int pv_g = 0, pv_i = 0, pv_st = 0;
-      bool pv_first = false, pv_last = false;
-      auto issue_pv = [&]() -> bool {
-        if (!mbar_wait(&p_full[pv_g & 1], (pv_g >> 1) & 1, wc, 5)) return false;
-        if (!mbar_wait(&v_full[pv_st], (pv_g / S) & 1, wc, 6)) return false;
-        if (pv_first && pv_i >= 1 && !mbar_wait(o_empty, (pv_i - 1) & 1, wc, 7)) return false;
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(smem + Cfg::kVOff + pv_st * Cfg::kTileBytes);
-        const uint32_t a_p = tmem + Cfg::kTmemP + (pv_g & 1) * (kBN / 2);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile.
-          // The leading-byte offset is the distance to the next 64-column block of B: the second
-          // half of V for d=128; for d=64 the ones tile (every B row of it is ones, whatever the
-          // swizzle, so each K step may read the same 2 KB)
-          const uint32_t sub = v_base + kk * 2048;
-          const uint32_t lbo = Cfg::kTcZ ? ones_base - sub : Cfg::kHalfBytes;
-          mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(sub, lbo, 1024), idO, (pv_first && kk == 0) ? 0u : 1u);
-        }
-        mma_commit(&v_empty[pv_st]);
-        mma_commit(&pv_done[pv_g & 1]);
-        if (pv_last) mma_commit(o_full);
-        have_prev = false;
-        return true;
-      };
       for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
         const Item it = item_at(p, idx);
-        if (have_prev) ok = issue_pv();  // finish the previous item before waiting on this one
-        if (ok) ok = mbar_wait(&q_full[i & 1], (i >> 1) & 1, wc, 3);
+        ok = mbar_wait(&q_full[i & 1], (i >> 1) & 1, wc, 3);
         const uint32_t q_base = smem_u32(smem + Cfg::kQOff + (i & 1) * Cfg::kTileBytes);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
           const int st = g % S;
           ok = mbar_wait(&k_full[st], (g / S) & 1, wc, 4);
+          // S[g % 2] still holds S_{g-2} until the pointwise group has read it (p_full)
+          if (ok && g >= 2) ok = mbar_wait(&p_full[g & 1], ((g - 2) >> 1) & 1, wc, 13);
           if (!ok) break;
           tc_fence_after();
           const uint32_t k_base = smem_u32(smem + Cfg::kKOff + st * Cfg::kTileBytes);
@@ -317,25 +280,57 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&s_full[g & 1]);
           mma_commit(&k_empty[st]);
           if (t == it.n_count - 1) mma_commit(&q_empty[i & 1]);
-          if (have_prev) ok = issue_pv();
-          if (!ok) break;
-          have_prev = true;
-          pv_g = g;
-          pv_i = i;
-          pv_st = st;
-          pv_first = t == 0;
-          pv_last = t == it.n_count - 1;
         }
       }
-      if (ok && have_prev) ok = issue_pv();
-      if (!ok) {
-        mma_commit(drain);  // wait for every MMA in flight before TMEM is released
+      if (!ok) {  // wait for this thread's products in flight before TMEM is released
+        mma_commit(drain);
         mbar_wait_drain(drain, 0);
       }
     }
     __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------------------------------------------------ O += P V issuer
+    if (elect_one()) {
+      // O (and for d=64 Z): A TMEM, B MN-major, N = D (+16 ones columns)
+      constexpr uint32_t idO = idesc_f16(1, 0, 1, Cfg::kTcZ ? D + 16 : D, kBM);
+      const uint32_t ones_base = smem_u32(smem + Cfg::kOnesOff);
+      bool ok = true;
+      int g = 0, i = 0;
+      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+        const Item it = item_at(p, idx);
+        for (int t = 0; t < it.n_count && ok; ++t, ++g) {
+          const int st = g % S;
+          ok = mbar_wait(&p_full[g & 1], (g >> 1) & 1, wc, 5);
+          if (ok) ok = mbar_wait(&v_full[st], (g / S) & 1, wc, 6);
+          // the first product of an item overwrites O: the previous item's epilogue must have read it
+          if (ok && t == 0 && i >= 1) ok = mbar_wait(o_empty, (i - 1) & 1, wc, 7);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t v_base = smem_u32(smem + Cfg::kVOff + st * Cfg::kTileBytes);
+          const uint32_t a_p = tmem + Cfg::kTmemP + (g & 1) * (kBN / 2);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            // 16 keys per step: 8 packed TMEM columns of P; 16 V rows = 2048 B of the MN-major tile.
+            // The leading-byte offset is the distance to the next 64-column block of B: the second
+            // half of V for d=128; for d=64 the ones tile (every B row of it is ones, whatever the
+            // swizzle, so each K step may read the same 2 KB)
+            const uint32_t sub = v_base + kk * 2048;
+            const uint32_t lbo = Cfg::kTcZ ? ones_base - sub : Cfg::kHalfBytes;
+            mma_ts(tmem + Cfg::kTmemO, a_p + kk * 8, sdesc_sw128(sub, lbo, 1024), idO, (t == 0 && kk == 0) ? 0u : 1u);
+          }
+          mma_commit(&v_empty[st]);
+          mma_commit(&pv_done[g & 1]);
+          if (t == it.n_count - 1) mma_commit(o_full);
+        }
+      }
+      if (!ok) {
+        mma_commit(drain + 1);
+        mbar_wait_drain(drain + 1, 0);
+      }
+    }
+    __syncwarp();
   } else {
-    // ------------------------------------------------------------------ pointwise warpgroups
+    // ------------------------------------------------------------------ pointwise warpgroups (warps 2-9)
     const int wg = (warp - 2) >> 2;
     const int lg = warp & 3;              // TMEM lane group of this warp
     const int row = lg * 32 + lane;       // query row within the tile == TMEM lane
@@ -575,10 +570,13 @@ bool tc_fwd_supported(const Problem& p) {
 int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (!get_encoder()) return FB_ERR_NO_DEVICE;
   CUtensorMap mq, mk, mv;
-  if (!encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D, kBM) || !encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D, kBN) ||
-      !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D, kBN))
+  const bool map3 = bh_mergeable(pr.q, pr.H) && bh_mergeable(pr.k, pr.H) && bh_mergeable(pr.v, pr.H);
+  if (!encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D, kBM, map3) ||
+      !encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D, kBN, map3) ||
+      !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D, kBN, map3))
     return FB_ERR_ALIGN;
   FwdParams fp{};
+  fp.map3 = map3;
   fp.B = pr.B; fp.H = pr.H; fp.T = pr.T;
   fp.n_mt = (pr.T + kBM - 1) / kBM;
   fp.n_items = fp.n_mt * pr.B * pr.H;

@@ -32,15 +32,26 @@ bool tma_ok(const Tensor4& t) {
   return true;
 }
 
-// 4-D map: dims (D, T, H, B), box (64, box_rows, 1, 1), 128-byte swizzle.  Rows at or beyond T
-// read as zeros (per head, since T is its own dimension).
-bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows) {
+// (B, H) can be addressed as one dimension of B*H when the batch stride is H head strides.
+bool bh_mergeable(const Tensor4& t, int H) { return t.s[0] == (int64_t)H * t.s[1]; }
+
+// Map over a (B, H, T, D) bf16 tensor with box (64, box_rows) of 128-byte-swizzled rows.  With
+// merge_bh the map is 3-D, dims (D, T, B*H), coordinates (x, row, b*H + h); otherwise 4-D, dims
+// (D, T, H, B).  A TMA copy through a 3-D map takes less time than through a 4-D one.  Rows at or
+// beyond T read as zeros (per head, since T is its own dimension).
+bool encode_bhtd(CUtensorMap* m, const Tensor4& t, int B, int H, int T, int D, int box_rows, bool merge_bh) {
   if (!get_encoder()) return false;
+  if (merge_bh && !bh_mergeable(t, H)) return false;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)t.s[2] * 2, (cuuint64_t)t.s[1] * 2, (cuuint64_t)t.s[0] * 2};
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(t.ptr), dims, strides, box, estr,
+  cuuint32_t rank = 4;
+  if (merge_bh) {
+    dims[2] = (cuuint64_t)B * H;
+    rank = 3;
+  }
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(t.ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;

@@ -108,13 +108,19 @@ def test_tc_forward_is_selected_for_bf16_d64_d128():
     assert _lib.load().fb_select_path(ctypes.byref(a), 0) == _lib.FB_PATH_GENERAL
 
 
-BWD_CASES = [c for c in CASES if c[3] == 64]
+# every forward case, plus shapes where CTAs walk several work items (windows of heads in the
+# key-major kernel, LPT rounds in the query-major one) for both head dims
+BWD_CASES = CASES + [
+    (4, 8, 1024, 64, True, 0, None),
+    (2, 3, 1536, 128, True, 0, None),
+    (3, 5, 640, 64, False, 0, None),
+]
 
 
 @pytest.mark.parametrize("purified", [False, True])
 @pytest.mark.parametrize("case", BWD_CASES, ids=[str(c) for c in BWD_CASES])
 def test_tc_backward_matches_oracle(case, purified):
-    """Forward and backward both forced onto the tcgen05 kernels (d=64), against the oracle."""
+    """Forward and backward both forced onto the tcgen05 kernels (d=64 and d=128), against the oracle."""
     from parity_util import check_all, run_cuda, run_oracle
 
     B, H, T, D, causal, window, doc_mean = case

@@ -83,8 +83,9 @@ def test_static_scratch_refuses_problems_over_the_limit():
     dq, dk, dv = (torch.empty_like(p["q"]) for _ in range(3))
     dscale = torch.zeros(1, device="cuda")
     a = _args(p, dq, dk, dv, dscale)
-    # claim a C2-sized problem: its backward needs ~70 MB of scratch; refused before any launch
-    a.batch, a.heads, a.seq_len = 8, 16, 2048
+    # claim B=8, H=16, N=32768: its backward needs ~34 MB of scratch (two fp32 vectors per query
+    # row and the parameter partials); refused before any launch
+    a.batch, a.heads, a.seq_len = 8, 16, 32768
     assert lib.fb_bwd_workspace_size(ctypes.byref(a)) > _lib.FB_STATIC_SCRATCH_BYTES
     rc = lib.fb_born_bwd_static_scratch(ctypes.byref(a), torch.cuda.current_stream().cuda_stream)
     assert rc == _lib.FB_ERR_SCRATCH_LIMIT
