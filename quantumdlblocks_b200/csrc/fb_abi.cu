@@ -75,6 +75,7 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, b
   p->causal = a->is_causal != 0; p->window = a->window_size;
   p->eps = a->eps; p->eps_base = a->eps_base;
   p->purified = purified;
+  p->deterministic = a->deterministic != 0;
   if (a->scale == nullptr) return FB_ERR_ARG;
   if (a->scale_numel != 1 && a->scale_numel != p->H) return FB_ERR_ARG;
   p->scale = a->scale; p->scale_per_head = a->scale_numel > 1;
@@ -114,15 +115,21 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, b
   return FB_OK;
 }
 
+// Tensor-core backward: the fused kernel for d = 64 (its dQ partials are added by fp32
+// reduce-adds, in an order that can vary); the two-kernel backward for d = 128 and whenever the
+// caller asks for deterministic gradients.
+bool use_fused_bwd(const Problem& p) { return p.D == 64 && !p.deterministic && tc_bwd64_supported(p); }
+
 int choose_path(const fb_attn_args* a, const Problem& p, bool backward) {
-  const bool tc = backward ? tc_bwd_supported(p) : tc_fwd_supported(p);
+  const bool tc = backward ? (use_fused_bwd(p) || tc_bwd_supported(p)) : tc_fwd_supported(p);
   if (a->path == FB_PATH_GENERAL) return FB_PATH_GENERAL;
   if (a->path == FB_PATH_TCGEN05) return tc ? FB_PATH_TCGEN05 : -FB_ERR_UNSUPPORTED;
   return tc ? FB_PATH_TCGEN05 : FB_PATH_GENERAL;
 }
 
 size_t workspace_for(const Problem& p, int path) {
-  return path == FB_PATH_TCGEN05 ? tc_bwd_workspace(p) : general_bwd_workspace(p);
+  if (path != FB_PATH_TCGEN05) return general_bwd_workspace(p);
+  return use_fused_bwd(p) ? tc_bwd64_workspace(p) : tc_bwd_workspace(p);
 }
 
 int run(const fb_attn_args* a, void* stream, bool purified, bool backward) {
@@ -142,7 +149,8 @@ int run(const fb_attn_args* a, void* stream, bool purified, bool backward) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int launches = 0;
   if (path == FB_PATH_TCGEN05) {
-    rc = backward ? tc_bwd(p, s, &launches) : tc_fwd(p, s, &launches);
+    rc = backward ? (use_fused_bwd(p) ? tc_bwd64(p, s, &launches) : tc_bwd(p, s, &launches))
+                  : tc_fwd(p, s, &launches);
   } else {
     rc = backward ? general_bwd(p, s, &launches) : general_fwd(p, s, &launches);
   }

@@ -29,6 +29,7 @@ struct Problem {
   int window;
   float eps, eps_base;
   bool purified;
+  bool deterministic;  // backward without floating-point atomics
   Tensor4 q, k, v, o, dout, dq, dk, dv;
   float* z;
   const float* scale;
@@ -65,11 +66,10 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(flo
 //   causal: j <= i;  window > 0: i - j < window (a non-causal window leaves the future visible);
 //   document ids: equal.  Keys at or beyond T are never valid.
 // ------------------------------------------------------------------------------------------
+//   Written with non-short-circuit & / | so that it compiles to predicate logic: the row index
+//   differs between the lanes of a warp, and a short-circuit form becomes divergent branches.
 __device__ __forceinline__ bool pair_valid(int i, int j, int T, bool causal, int window, int doc_i, int doc_j) {
-  bool ok = j < T;
-  if (causal) ok = ok && (j <= i);
-  if (window > 0) ok = ok && (i - j < window);
-  return ok && (doc_i == doc_j);
+  return (j < T) & (!causal | (j <= i)) & ((window <= 0) | (i - j < window)) & (doc_i == doc_j);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -160,9 +160,12 @@ int general_bwd(const Problem& p, cudaStream_t s, int* launches);
 size_t general_bwd_workspace(const Problem& p);
 bool tc_fwd_supported(const Problem& p);
 int tc_fwd(const Problem& p, cudaStream_t s, int* launches);
-bool tc_bwd_supported(const Problem& p);
+bool tc_bwd_supported(const Problem& p);   // two-kernel backward (fb_tc_bwd.cu), d = 64 or 128
 int tc_bwd(const Problem& p, cudaStream_t s, int* launches);
 size_t tc_bwd_workspace(const Problem& p);
+bool tc_bwd64_supported(const Problem& p);  // fused backward (fb_tc_bwd64.cu), d = 64
+int tc_bwd64(const Problem& p, cudaStream_t s, int* launches);
+size_t tc_bwd64_workspace(const Problem& p);
 void record_cuda_error(cudaError_t e);
 // TMA tensor maps (fb_tmap.cu)
 bool get_encoder();

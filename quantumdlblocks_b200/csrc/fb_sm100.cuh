@@ -136,6 +136,21 @@ __device__ __forceinline__ void tma_load_bhtd(void* dst, const CUtensorMap* map,
   else
     tma_load_4d(dst, map, bar, x, row, h, b);
 }
+// Tiled TMA store shared -> global through a map built by encode_bhtd (3-D merged b*H + h, or
+// 4-D), tracked by the bulk async-group; rows at or beyond the tensor's T are not written.
+__device__ __forceinline__ void tma_store_bhtd(const CUtensorMap* map, const void* src, bool map3, int x, int row, int h,
+                                               int b, int H) {
+  if (map3)
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(row), "r"(b * H + h), "r"(smem_u32(src))
+                 : "memory");
+  else
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(row), "r"(h), "r"(b), "r"(smem_u32(src))
+                 : "memory");
+}
 // 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16)
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

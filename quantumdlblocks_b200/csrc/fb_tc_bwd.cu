@@ -25,13 +25,15 @@
 //   dV += W^T dO, dK += G^T Q                            (key-major kernel)
 //   S = Q K^T, dP = dO V^T, pointwise G, dQ += G K       (query-major kernel)
 //
-// Warps (352 threads, both main kernels): 0 TMA producers (copies issued by one thread complete
+// Warps (384 threads, both main kernels): 0 TMA producers (copies issued by one thread complete
 // one after another, about 0.3 us each, so each operand stream has its own lane), 1 TMEM owner +
-// score-product issuer, 2-9 two pointwise warpgroups (group g takes the tiles t with t % 2 == g),
-// 10 gradient-product issuer.  One thread issues a tcgen05.mma at most every ~50 cycles, about
-// the execution time of an N = 64 product, so the two kinds of product are issued by two warps.
-// The score issuer runs up to kNB - 1 tiles ahead of the gradient issuer (kNB TMEM buffers), so
-// a group finds its next tile's scores ready when it finishes the current one.
+// issuer of the raw-score product (S^T / S), 2-9 two pointwise warpgroups (group g takes the
+// tiles t with t % 2 == g), 10 issuer of the dO.v product (dP^T / dP), 11 issuer of the gradient
+// products.  One thread issues a tcgen05.mma at most every ~50 cycles (a commit costs about as
+// much), about the execution time of an N = 64 product, so each product has its own issuing
+// warp; barriers that both score products feed count two arrivals.  The score issuers run up to
+// kNB - 1 tiles ahead of the gradient issuer (kNB TMEM buffers), so a group finds its next
+// tile's scores ready when it finishes the current one.
 //
 // TMEM columns, key-major kernel:   d=64  S^T[3] 0/64/128, dP^T[3] 192/256/320, dV 384, dK 448
 //                                   d=128 S^T[2] 0/64, dP^T[2] 128/192, dV 256, dK 384
@@ -49,7 +51,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 352;  // 11 warps
+constexpr int kThreads = 384;  // 12 warps
 constexpr uint32_t kTmemCols = 512;
 constexpr int kRowPad = 128;  // per-head rows of the prep vectors are padded to this
 
@@ -120,7 +122,7 @@ struct KvCfg {
   static constexpr uint32_t kTS = 0, kTdP = kNB * 64, kTdV = 2 * kNB * 64, kTdK = kTdV + D;
   static_assert(kTdK + D <= kTmemCols, "TMEM columns");
   static_assert(kSmem + 1024 <= 227 * 1024, "shared memory per CTA");
-  static_assert(4 + 4 * kQS + 3 * kNB + 4 <= 60, "barrier area");
+  static_assert(4 + 4 * kQS + 3 * kNB + 5 <= 60, "barrier area");
 };
 
 struct BwdItem {
@@ -215,17 +217,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);  // both score products
     }
     for (int i = 0; i < NB; ++i) {
-      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_full[i], 2);  // S^T and dP^T
       mbar_init(&wg_full[i], 128);
       mbar_init(&mma_done[i], 1);
     }
     mbar_init(acc_full, 1);
     mbar_init(acc_empty, 256);
-    mbar_init(drain, 1);
-    mbar_init(drain + 1, 1);
+    for (int r = 0; r < 3; ++r) mbar_init(drain + r, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -306,9 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1 || warp == 10) {
+  } else if (warp == 1 || warp >= 10) {
     // ------------------------------------------------------------------ MMA issuers
-    // warp 1: S^T, dP^T (score cursor); warp 10: dV, dK (gradient cursor)
+    // warp 1: S^T, warp 10: dP^T (score cursor); warp 11: dV, dK (gradient cursor)
     if (elect_one()) {
       constexpr uint32_t idSdP = idesc_f16(1, 0, 0, BM, C::kBN);  // M = 128 keys, N = 64 queries
       constexpr uint32_t idAcc = idesc_f16(1, 0, 1, D, C::kBN);   // A TMEM, B MN-major, N = D
@@ -320,31 +321,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       BwdItem s_it, u_it;
       bool s_have = bwd_next(p, s_k, s_it);
       bool u_have = bwd_next(p, u_k, u_it);
-      auto issue_sdp = [&]() -> bool {
+      // which = 0: S^T = K Q^T into S^T[b]; which = 1: dP^T = V dO^T into dP^T[b]
+      auto issue_sdp = [&](int which) -> bool {
         const int b = s_g % NB;
         const int qs = s_g % QS;
         const int kb = s_i % KVB;
         if (s_t == 0 && !mbar_wait(&kv_full[kb], (s_i / KVB) & 1, wc, 22)) return false;
-        if (!mbar_wait(&q_full[qs], (s_g / QS) & 1, wc, 23)) return false;
-        if (!mbar_wait(&o_full[qs], (s_g / QS) & 1, wc, 28)) return false;
+        if (!mbar_wait(which == 0 ? &q_full[qs] : &o_full[qs], (s_g / QS) & 1, wc, 23 + 5 * which)) return false;
         // buffer b is free once the gradient products of tile s_g - NB have read W^T / G^T
         if (s_g >= NB && !mbar_wait(&mma_done[b], ((s_g / NB) - 1) & 1, wc, 24)) return false;
         tc_fence_after();
-        const uint64_t dK = sdesc_sw128(smem_u32(smem + C::kSK + kb * C::kKTile), 16, 1024);
-        const uint64_t dV = sdesc_sw128(smem_u32(smem + C::kSV + kb * C::kKTile), 16, 1024);
-        const uint64_t dQ = sdesc_sw128(smem_u32(smem + C::kSQ + qs * C::kQTile), 16, 1024);
-        const uint64_t ddO = sdesc_sw128(smem_u32(smem + C::kSdO + qs * C::kQTile), 16, 1024);
+        const uint64_t dA = sdesc_sw128(smem_u32(smem + (which ? C::kSV : C::kSK) + kb * C::kKTile), 16, 1024);
+        const uint64_t dB = sdesc_sw128(smem_u32(smem + (which ? C::kSdO : C::kSQ) + qs * C::kQTile), 16, 1024);
+        const uint32_t dst = tmem + (which ? C::kTdP : C::kTS) + b * 64;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {  // 16 head-dim elements per step (32 B along a row)
           const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
           const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + C::kTS + b * 64, dK + ok_, dQ + oq_, idSdP, kk > 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
-          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + C::kTdP + b * 64, dV + ok_, ddO + oq_, idSdP, kk > 0);
+          mma_ss(dst, dA + ok_, dB + oq_, idSdP, kk > 0);
         }
         mma_commit(&sdp_full[b]);
         // K and V feed only the score products: the item's buffer is free after its last one
@@ -387,9 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
-      const int role = warp == 1 ? 0 : 1;
-      if (role == 0) {
-        while (ok && s_have) ok = issue_sdp();
+      const int role = warp == 1 ? 0 : warp - 9;  // 0: S^T, 1: dP^T, 2: dV / dK
+      if (role < 2) {
+        while (ok && s_have) ok = issue_sdp(role);
       } else {
         while (ok && u_have) ok = issue_grads();
       }
@@ -452,12 +446,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool full = !kHasDoc && (!p.causal || m0 >= n0 + C::kBN - 1) &&
                           (p.window <= 0 || (m0 + BM - 1) - n0 < p.window) && (m0 + BM <= p.T) &&
                           (n0 + C::kBN <= p.T);
-        // causal diagonal tiles (m0 = n0 or n0 + 64, all keys < T): for query chunk c of warp lg,
-        // with d = 32 c + (m0 - n0) - 32 lg, query column e is valid iff e + d >= lane
-        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 + C::kBN <= p.T;
         const float4* zd4 = reinterpret_cast<const float4*>(vzd + qs * 2 * BM);  // (z, d) of two queries each
         const uint32_t s_col = lane_addr + C::kTS + b * 64, p_col = lane_addr + C::kTdP + b * 64;
-        // one 16-query sub-chunk of a fully valid tile: W^T, G^T -> TMEM over consumed columns
+        // Partial tiles: the raw score of every invalid pair is replaced by NaN before the map,
+        // which turns it into p = 0 and dL/draw = 0 (fmaxf returns its non-NaN operand and no
+        // other term of these maps touches raw), so one branch-free body serves every tile.
+        const int lo_q = p.causal ? kj - m0 : -BM;  // causal: query column qx is valid iff qx >= kj - m0
+        const int hi_q = kj < p.T ? p.T - m0 : 0;   // queries below T; a padded key row has none
+        auto mask16 = [&](int sc, uint32_t (&rs)[16]) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int qx = sc * 16 + e;
+            bool v = (qx >= lo_q) & (qx < hi_q) & ((p.window <= 0) | ((m0 + qx) - kj < p.window));
+            if constexpr (kHasDoc) v = v & (docq[qx] == doc_j);
+            rs[e] = v ? rs[e] : 0x7FC00000u;
+          }
+        };
+        // one 16-query sub-chunk: W^T, G^T -> TMEM over the consumed S^T / dP^T columns
         auto sub16 = [&](int sc, const uint32_t (&rs)[16], const uint32_t (&rd)[16]) {
           float zc[16], dc[16];
 #pragma unroll
@@ -481,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st8(s_col + sc * 8, wpk);
           tmem_st8(p_col + sc * 8, gpk);
         };
-        if (full) {
+        {
           // software pipeline: the TMEM loads of sub-chunk s+1 are in flight while s is computed
           uint32_t sA[16], dA[16], sB[16], dB[16];
           tmem_ld16(s_col, sA);
@@ -491,73 +496,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int sc = 0; sc < BM / 16; sc += 2) {
             tmem_ld16(s_col + (sc + 1) * 16, sB);
             tmem_ld16(p_col + (sc + 1) * 16, dB);
+            if (!full) mask16(sc, sA);
             sub16(sc, sA, dA);
             tmem_wait_ld();
             if (sc + 2 < BM / 16) {
               tmem_ld16(s_col + (sc + 2) * 16, sA);
               tmem_ld16(p_col + (sc + 2) * 16, dA);
             }
+            if (!full) mask16(sc + 1, sB);
             sub16(sc + 1, sB, dB);
             tmem_wait_ld();
           }
-        }
-#pragma unroll 1
-        for (int c = 0; c < (full ? 0 : BM / 32); ++c) {
-          uint32_t wpk[16], gpk[16];
-          const int d = 32 * c + (m0 - n0) - 32 * lg;
-          if (diag && d <= -32) {  // every key of this warp is after every query of the chunk
-#pragma unroll
-            for (int e = 0; e < 16; ++e) wpk[e] = gpk[e] = 0u;
-          } else {
-            uint32_t rs[32], rd[32];
-            tmem_ld32(s_col + c * 32, rs);
-            tmem_ld32(p_col + c * 32, rd);
-            float zc[32], dc[32];  // per-query 1/Z and delta/Z of these 32 columns (shared, broadcast)
-#pragma unroll
-            for (int v2 = 0; v2 < 16; ++v2) {
-              const float4 f = zd4[c * 16 + v2];
-              zc[2 * v2] = f.x; dc[2 * v2] = f.y; zc[2 * v2 + 1] = f.z; dc[2 * v2 + 1] = f.w;
-            }
-            tmem_wait_ld();
-            if (diag && d >= 31) {
-#pragma unroll
-              for (int e = 0; e < 32; e += 2) {
-                float wv[2], gv[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const float raw = __uint_as_float(rs[e + u]);
-                  wv[u] = map.prob(raw, true) * zc[e + u];
-                  gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
-                }
-                wpk[e / 2] = pack2<true>(wv[0], wv[1]);
-                gpk[e / 2] = pack2<true>(gv[0], gv[1]);
-              }
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; e += 2) {
-                float wv[2], gv[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                  const int qx = c * 32 + e + u;
-                  bool valid;
-                  if (diag) {
-                    valid = e + u + d >= lane;
-                  } else {
-                    int doc_i = 0;
-                    if constexpr (kHasDoc) doc_i = docq[qx];
-                    valid = pair_valid(m0 + qx, kj, p.T, p.causal, p.window, doc_i, doc_j);
-                  }
-                  const float raw = __uint_as_float(rs[e + u]);
-                  wv[u] = map.prob(raw, valid) * zc[e + u];
-                  gv[u] = map.grad(raw, valid, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
-                }
-                wpk[e / 2] = pack2<true>(wv[0], wv[1]);
-                gpk[e / 2] = pack2<true>(gv[0], gv[1]);
-              }
-            }
-          }
-          tmem_st16(s_col + c * 16, wpk);  // W^T over the consumed S^T columns
-          tmem_st16(p_col + c * 16, gpk);  // G^T over the consumed dP^T columns
         }
         tmem_wait_st();
         tc_fence_before();
@@ -649,7 +598,7 @@ struct DqCfg {
   static constexpr uint32_t kTS = 0, kTdP = kNB * 64, kTdQ = 2 * kNB * 64;
   static_assert(kTdQ + D <= kTmemCols, "TMEM columns");
   static_assert(kSmem + 1024 <= 227 * 1024, "shared memory per CTA");
-  static_assert(4 + 2 * kKS + 2 * kVS + 3 * kNB + 4 <= 60, "barrier area");
+  static_assert(4 + 2 * kKS + 2 * kVS + 3 * kNB + 5 <= 60, "barrier area");
 };
 
 struct QItem {
@@ -707,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);  // Q by the S product, dO by the dP product
     }
     for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
@@ -718,14 +667,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < NB; ++i) {
-      mbar_init(&s_full[i], 1);
+      mbar_init(&s_full[i], 2);  // S and dP
       mbar_init(&g_full[i], 128);
       mbar_init(&mma_done[i], 1);
     }
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 256);
-    mbar_init(drain, 1);
-    mbar_init(drain + 1, 1);
+    for (int r = 0; r < 3; ++r) mbar_init(drain + r, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -797,9 +745,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1 || warp == 10) {
+  } else if (warp == 1 || warp >= 10) {
     // ------------------------------------------------------------------ MMA issuers
-    // warp 1: S, dP (score cursor); warp 10: dQ += G K (gradient cursor)
+    // warp 1: S, warp 10: dP (score cursor); warp 11: dQ += G K (gradient cursor)
     if (elect_one()) {
       constexpr uint32_t idS = idesc_f16(1, 0, 0, BN, C::kBM);  // M = 128 queries, N = 64 keys
       constexpr uint32_t idQ = idesc_f16(1, 0, 1, D, C::kBM);   // A TMEM (G), B MN-major (K), N = D
@@ -810,33 +758,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool s_have = s_idx < p.n_qitems, u_have = u_idx < p.n_qitems;
       if (s_have) s_it = q_item(p, s_idx);
       if (u_have) u_it = q_item(p, u_idx);
-      auto issue_sdp = [&]() -> bool {
+      // which = 0: S = Q K^T into S[b]; which = 1: dP = dO V^T into dP[b]
+      auto issue_sdp = [&](int which) -> bool {
         const int b = s_g % NB;
         const int qb = s_i % QB;
         if (s_t == 0 && !mbar_wait(&q_full[qb], (s_i / QB) & 1, wc, 43)) return false;
-        if (!mbar_wait(&k_full[s_g % KS], (s_g / KS) & 1, wc, 44)) return false;
-        if (!mbar_wait(&v_full[s_g % VS], (s_g / VS) & 1, wc, 45)) return false;
+        if (which == 0 && !mbar_wait(&k_full[s_g % KS], (s_g / KS) & 1, wc, 44)) return false;
+        if (which == 1 && !mbar_wait(&v_full[s_g % VS], (s_g / VS) & 1, wc, 45)) return false;
         // buffer b is free once dQ += G K of tile s_g - NB has read G
         if (s_g >= NB && !mbar_wait(&mma_done[b], ((s_g / NB) - 1) & 1, wc, 46)) return false;
         tc_fence_after();
-        const uint64_t dQ = sdesc_sw128(smem_u32(smem + C::kSQ + qb * C::kQTile), 16, 1024);
-        const uint64_t ddO = sdesc_sw128(smem_u32(smem + C::kSdO + qb * C::kQTile), 16, 1024);
-        const uint64_t dK = sdesc_sw128(smem_u32(smem + C::kSK + (s_g % KS) * C::kKTile), 16, 1024);
-        const uint64_t dV = sdesc_sw128(smem_u32(smem + C::kSV + (s_g % VS) * C::kKTile), 16, 1024);
+        const uint64_t dA = sdesc_sw128(smem_u32(smem + (which ? C::kSdO : C::kSQ) + qb * C::kQTile), 16, 1024);
+        const uint64_t dB = sdesc_sw128(
+            smem_u32(smem + (which ? C::kSV + (s_g % VS) * C::kKTile : C::kSK + (s_g % KS) * C::kKTile)), 16, 1024);
+        const uint32_t dst = tmem + (which ? C::kTdP : C::kTS) + b * 64;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
           const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + C::kTS + b * 64, dQ + oq_, dK + ok_, idS, kk > 0);
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t oq_ = ((kk >> 2) * C::kQHalf + (kk & 3) * 32) >> 4;
-          const uint32_t ok_ = ((kk >> 2) * C::kKHalf + (kk & 3) * 32) >> 4;
-          mma_ss(tmem + C::kTdP + b * 64, ddO + oq_, dV + ok_, idS, kk > 0);
+          mma_ss(dst, dA + oq_, dB + ok_, idS, kk > 0);
         }
         mma_commit(&s_full[b]);
-        mma_commit(&v_empty[s_g % VS]);
+        if (which == 1) mma_commit(&v_empty[s_g % VS]);  // V feeds only dP
         if (s_t == s_it.n_count - 1) mma_commit(&q_empty[qb]);  // Q and dO feed only the score products
         ++s_g;
         if (++s_t == s_it.n_count) {
@@ -872,9 +815,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
-      const int role = warp == 1 ? 0 : 1;
-      if (role == 0) {
-        while (ok && s_have) ok = issue_sdp();
+      const int role = warp == 1 ? 0 : warp - 9;  // 0: S, 1: dP, 2: dQ
+      if (role < 2) {
+        while (ok && s_have) ok = issue_sdp(role);
       } else {
         while (ok && u_have) ok = issue_dq();
       }
@@ -936,40 +879,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool full = !kHasDoc && (!p.causal || n0 + BN - 1 <= it.m0) &&
                           (p.window <= 0 || (it.m0 + C::kBM - 1) - n0 < p.window) && (n0 + BN <= p.T);
         const uint32_t s_col = lane_addr + C::kTS + b * 64, p_col = lane_addr + C::kTdP + b * 64;
-        // two 32-key chunks; chunk c writes G (16 packed columns) over S columns [16c, 16c + 16),
-        // which chunk 0 has already read
+        // Partial tiles: invalid pairs get raw = NaN before the map, which yields dL/draw = 0
+        // (fmaxf returns its non-NaN operand), so one branch-free body serves every tile.
+        // Two 32-key chunks; chunk c writes G (16 packed columns) over S columns [16c, 16c + 16),
+        // which chunk 0 has already read.
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t rs[32], rd[32];
           tmem_ld32(s_col + c * 32, rs);
           tmem_ld32(p_col + c * 32, rd);
           tmem_wait_ld();
-          uint32_t gpk[16];
-          if (full) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float gv[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-                gv[u] = map.grad(__uint_as_float(rs[e + u]), true, fmaf(__uint_as_float(rd[e + u]), zinv, -dlz),
-                                 unused1, unused2);
-              gpk[e / 2] = pack2<true>(gv[0], gv[1]);
-            }
-          } else {
+          if (!full) {
             const int kbase = n0 + c * 32;
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float gv[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                int doc_j = 0;
-                if constexpr (kHasDoc) doc_j = docs_k[c * 32 + e + u];
-                const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
-                gv[u] = map.grad(__uint_as_float(rs[e + u]), valid, fmaf(__uint_as_float(rd[e + u]), zinv, -dlz),
-                                 unused1, unused2);
-              }
-              gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+            for (int e = 0; e < 32; ++e) {
+              int doc_j = 0;
+              if constexpr (kHasDoc) doc_j = docs_k[c * 32 + e];
+              const bool v = pair_valid(qi, kbase + e, p.T, p.causal, p.window, doc_i, doc_j);
+              rs[e] = v ? rs[e] : 0x7FC00000u;
             }
+          }
+          uint32_t gpk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float gv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              gv[u] = map.grad(__uint_as_float(rs[e + u]), true, fmaf(__uint_as_float(rd[e + u]), zinv, -dlz), unused1,
+                               unused2);
+            gpk[e / 2] = pack2<true>(gv[0], gv[1]);
           }
           tmem_st16(s_col + c * 16, gpk);
         }

@@ -1,0 +1,938 @@
+// fb_tc_bwd64.cu -- fused flash-Born backward on the tcgen05 tensor cores (sm_100a), head dim 64.
+//
+// One key-major kernel computes dK, dV and the dQ partials of each (key tile, query tile): five
+// products per tile and no recomputation.  dQ partials are reduced into an fp32 accumulator by TMA
+// tensor reduce-add, so the order of the additions (and the last bits of dQ) can vary between
+// runs; callers that ask for deterministic gradients get the two-kernel backward of fb_tc_bwd.cu,
+// which also serves head dim 128 (whose accumulators do not fit in TMEM next to dQ's).
+//
+// Three launches (all on the caller's stream):
+//   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
+//                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
+//   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
+//                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
+//                        tiles that can hold valid
+//                        pairs and accumulates dK, dV in TMEM; dQ partials are reduced into the
+//                        fp32 accumulator with TMA tensor reduce-add.  The query-tile pipeline
+//                        runs on across items (K, V double-buffered per item)
+//   3. bwd_post_kernel   dQ = accumulator -> input dtype
+//   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
+//                        sums and the main kernel's per-CTA partials
+//
+// Per (key tile, query tile) the main kernel runs the five products the algorithm needs
+// (the reference's two kernels run six, flash_born.py:267-312 and :398-427):
+//   S^T  = K Q^T        M=128 keys, N=64 queries, K=64   A=K (smem K-major), B=Q (smem K-major)
+//   dP^T = V dO^T       same shape                        A=V, B=dO
+//   pointwise (thread = key row): a = relu(scale raw), p = a^2, W = p / Z_i,
+//     dP = (dP^T - delta_i) / Z_i, G = dL/draw = 2 a dP scale (masked; purified: 4u^3 dP gamma +
+//     2 eps_base b dP) -> W^T, G^T into TMEM (bf16, aliasing S^T / dP^T) and G into smem
+//   dV  += W^T dO       M=128, N=64, K=64 queries         A=W^T (TMEM), B=dO (smem MN-major)
+//   dK  += G^T Q        same                              A=G^T (TMEM), B=Q (smem MN-major)
+//   dQ_t = G K          M=64 queries, N=64, K=128 keys    A=G (smem MN-major), B=K (smem MN-major)
+//
+// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-9 two pointwise warpgroups
+// (key rows; group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two
+// groups' latency chains interleave).  Before each tile a group drains the dQ partial of its
+// previous tile (TMEM -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator).  S^T/dP^T/dQ are double-buffered in TMEM so
+// the products of query tile t+1 overlap the pointwise work of tile t.
+//
+// TMEM columns: S^T[0..1] 0/64, dP^T[0..1] 128/192, dV 256, dK 320, dQ[0..1] 384/448.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "fb_common.cuh"
+#include "fb_sm100.cuh"
+
+namespace fb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBN = 128;  // keys per CTA
+constexpr int kBM = 64;   // queries per step
+constexpr int kD = 64;
+constexpr int kThreads = 384;  // 12 warps
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTS = 0, kTdP = 128, kTdV = 256, kTdK = 320, kTdQ = 384;
+
+// shared memory carve-up (bytes from the 1024-aligned base)
+constexpr uint32_t kSK = 0;                    // K tiles [2 items] 128 x 64 bf16, 32 KB apart (K, V interleaved)
+constexpr uint32_t kSV = 16384;                // V tiles [2 items]
+constexpr int kQS = 3;                         // Q / dO / vector stages
+constexpr uint32_t kSQ = 65536;                // Q stages [kQS] 64 x 64     8 KB each
+constexpr uint32_t kSdO = kSQ + kQS * 8192;    // dO stages [kQS]            8 KB each
+constexpr uint32_t kSG = kSdO + kQS * 8192;    // G [4] 128 keys x 64 q      16 KB each (tile g uses g % 4)
+constexpr uint32_t kSStg = kSG + 4 * 16384;    // dQ staging [4 quadrants][2 groups] two 16 x 32 fp32 swizzled boxes
+constexpr uint32_t kSVec = kSStg + 32768;      // dlz[kQS][64] (delta / Z), zinv[kQS][64] (1 / Z) fp32
+constexpr uint32_t kSDoc = kSVec + kQS * 512;  // query doc ids [8 warps][64] int32
+constexpr uint32_t kSBar = kSDoc + 2048;       // barriers + flags
+constexpr uint32_t kSmemBytes = kSBar + 512;
+static_assert(kSmemBytes + 1024 <= 227 * 1024, "shared memory per CTA");
+
+struct BwdParams {
+  int B, H, T, Tpad;
+  int causal, window;
+  float eps_base;
+  const float* scale;
+  int scale_per_head;
+  const float* tau;
+  int tau_per_head;
+  const int32_t* doc;
+  int64_t doc_s0, doc_s1;
+  __nv_bfloat16* dk;
+  int64_t dk_s0, dk_s1, dk_s2;
+  __nv_bfloat16* dv;
+  int64_t dv_s0, dv_s1, dv_s2;
+  const float* dlz;    // [BH][Tpad]  delta_i / Z_i
+  const float* zinv;   // [BH][Tpad]  1 / Z_i
+  float* dq_acc;       // [BH][Tpad][64]
+  float* partials;     // [BH][n_kv][8 warps][2]
+  int n_kv, n_items;
+  int map3;            // tensor maps address (b, h) as one merged dimension
+  int* status;
+};
+
+template <class Map> struct BwdMap;
+template <> struct BwdMap<PlainMapNoParam> {
+  __device__ static PlainMapNoParam make(const BwdParams& p, int h) {
+    PlainMapNoParam m;
+    m.scale = p.scale[p.scale_per_head ? h : 0];
+    return m;
+  }
+};
+template <> struct BwdMap<PurifiedMapTC> {
+  __device__ static PurifiedMapTC make(const BwdParams& p, int h) {
+    PurifiedMapTC m;
+    m.gamma = p.scale[p.scale_per_head ? h : 0];
+    m.tau = p.tau[p.tau_per_head ? h : 0];
+    m.eps_base = p.eps_base;
+    return m;
+  }
+};
+
+struct BwdItem {
+  int b, h, kt, n0, m_first, n_tiles;
+};
+
+// Work item (bh, kt): keys [n0, n0 + kBN) of head bh; query tiles [m_first, m_first + 64 n_tiles)
+// can hold valid pairs for them.
+__device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int bh, int kt) {
+  BwdItem it;
+  it.kt = kt;
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  it.n0 = it.kt * kBN;
+  int lo = p.causal ? it.n0 : 0;
+  int hi = p.T;
+  if (p.window > 0) hi = min(p.T, it.n0 + kBN - 1 + p.window);
+  lo = (lo / kBM) * kBM;
+  it.m_first = lo;
+  it.n_tiles = hi > lo ? (hi - lo + kBM - 1) / kBM : 0;
+  return it;
+}
+
+// Schedule.  Items are numbered head-major, u = bh n_kv + kt, and the numbering is cut into
+// windows of 2 gridDim.x consecutive items (about 2 gridDim.x / n_kv heads).  Every item of a
+// head reads all of that head's Q, dO and 1/Z rows and reduce-adds into all of its fp32 dQ
+// accumulator rows, so while the CTAs work through one window only a few heads' rows are live
+// and they stay in L2 (ordering all key tile 0 items first keeps every head live at once, which
+// spills the accumulator to HBM).  Inside a window the items are sorted by key tile (under a
+// causal mask the early key tiles have the most query tiles) and dealt out as a snake: CTA c
+// takes window positions c and 2 gridDim.x - 1 - c, one long and one short item.
+// bwd_next: the item of this CTA's slot k, moving k past empty slots (the last window can be
+// short); false once the CTA has no items left.  Every role walks the same sequence.
+__device__ __forceinline__ bool bwd_next(const BwdParams& p, int& k, BwdItem& it) {
+  const int W = 2 * (int)gridDim.x;
+  for (;; ++k) {
+    const int a = (k >> 1) * W;  // first item of the window (n_items < 2^31)
+    if (a >= p.n_items) return false;
+    const int e = min(a + W, p.n_items);
+    int rem = (k & 1) ? W - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    if (rem >= e - a) continue;
+    // a = A n_kv + ra, e = E n_kv + re: the window holds key tile kt of heads
+    // A + [kt < ra] ..., (E - A) - [kt < ra] + [kt < re] of them
+    const int A = a / p.n_kv, ra = a - A * p.n_kv;
+    const int E = e / p.n_kv, re = e - E * p.n_kv;
+    for (int kt = 0; kt < p.n_kv; ++kt) {
+      const int c = (E - A) - (kt < ra ? 1 : 0) + (kt < re ? 1 : 0);
+      if (rem < c) {
+        it = bwd_item(p, A + (kt < ra ? 1 : 0) + rem, kt);
+        return true;
+      }
+      rem -= c;
+    }
+    return false;  // not reached: the per-key-tile counts add up to e - a
+  }
+}
+
+template <class Map, bool kHasDoc>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_bwd_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
+                  const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmdK,
+                  const __grid_constant__ CUtensorMap tmdV, const BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
+  uint64_t* kv_full = bars + 0;                // [2] per item parity
+  uint64_t* kv_empty = bars + 2;               // [2] (S^T / dP^T issuer and dQ issuer)
+  uint64_t* q_full = bars + 4;                 // [kQS] per query-tile stage: Q
+  uint64_t* o_full = q_full + kQS;             // [kQS] dO
+  uint64_t* vec_full = o_full + kQS;           // [kQS] delta / Z and 1 / Z (two copies)
+  uint64_t* q_empty = vec_full + kQS;          // [kQS] the whole stage
+  uint64_t* sdp_full = q_empty + kQS;          // [2] per query-tile parity
+  uint64_t* wg_full = sdp_full + 2;            // [2]
+  uint64_t* dvk_done = wg_full + 2;            // [2] dV, dK of the tile done: S^T / dP^T buffer free
+  uint64_t* dq_full = dvk_done + 2;            // [2]
+  uint64_t* dq_empty = dq_full + 2;            // [2]
+  uint64_t* acc_full = dq_empty + 2;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* drain = acc_full + 2;              // [3] one per MMA-issuing warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 4);
+  static_assert((4 + 4 * kQS + 10 + 2 + 3 + 2) * 8 <= 512, "barrier area");
+  float* vdlz = reinterpret_cast<float*>(smem + kSVec);                // [kQS][64]
+  float* vzinv = reinterpret_cast<float*>(smem + kSVec + kQS * 256);   // [kQS][64]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtx wc{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kQS; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&vec_full[i], 2);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 2);
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&wg_full[i], 128);
+      mbar_init(&dvk_done[i], 1);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], 128);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 256);
+    for (int r = 0; r < 3; ++r) mbar_init(drain + r, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmdO);
+    prefetch_tensormap(&tmDQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producers
+    // Copies issued by one thread complete one after another (about 0.3 us each), so the streams
+    // are split over lanes: lane 0 requests K / V of the items and Q of the query tiles, lane 1
+    // dO, lanes 2 and 3 the delta / Z and 1 / Z vectors; each walks the same tile sequence.
+    if (lane < 4) {
+      bool ok = true;
+      int g = 0, i = 0, kv_issued = 0, issued = 0;
+      uint64_t* full = lane == 0 ? q_full : (lane == 1 ? o_full : vec_full);
+      auto load_kv = [&](int item_seq, const BwdItem& it) -> bool {
+        const int kb = item_seq & 1;
+        if (item_seq >= 2 && !mbar_wait(&kv_empty[kb], ((item_seq >> 1) - 1) & 1, wc, 20)) return false;
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * kBN * kD * 2);
+        tma_load_bhtd(smem + kSK + kb * 32768, &tmK, &kv_full[kb], p.map3, 0, it.n0, it.h, it.b, p.H);
+        tma_load_bhtd(smem + kSV + kb * 32768, &tmV, &kv_full[kb], p.map3, 0, it.n0, it.h, it.b, p.H);
+        kv_issued = item_seq + 1;
+        return true;
+      };
+      int k = 0;
+      BwdItem it;
+      for (; ok && bwd_next(p, k, it); ++k, ++i) {
+        const int64_t bh = (int64_t)it.b * p.H + it.h;
+        if (lane == 0 && kv_issued <= i) ok = load_kv(i, it);
+        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
+          const int st = g % kQS;
+          if (g >= kQS) ok = mbar_wait(&q_empty[st], ((g / kQS) - 1) & 1, wc, 21);
+          if (!ok) break;
+          const int m0 = it.m_first + t * kBM;
+          if (lane < 2) {
+            mbar_arrive_expect_tx(&full[st], kBM * kD * 2);
+            tma_load_bhtd(smem + (lane == 0 ? kSQ : kSdO) + st * 8192, lane == 0 ? &tmQ : &tmdO, &full[st], p.map3, 0,
+                          m0, it.h, it.b, p.H);
+          } else {
+            mbar_arrive_expect_tx(&full[st], kBM * 4);
+            if (lane == 2)
+              bulk_load(vdlz + st * kBM, p.dlz + bh * p.Tpad + m0, kBM * 4, &full[st]);
+            else
+              bulk_load(vzinv + st * kBM, p.zinv + bh * p.Tpad + m0, kBM * 4, &full[st]);
+          }
+          issued = g + 1;
+          // once this item's first query tile is on its way, fetch the next item's K and V
+          if (lane == 0 && t == 0) {
+            int kn = k + 1;
+            BwdItem nit;
+            if (bwd_next(p, kn, nit)) ok = load_kv(i + 1, nit);
+          }
+        }
+      }
+      if (!ok) {
+        // abandoned: let this lane's copies already in flight land before the CTA exits (the
+        // vector barrier needs both vector lanes, so its wait may run to its bound)
+        for (int gg = max(0, issued - kQS); gg < issued; ++gg) mbar_wait_drain(&full[gg % kQS], (gg / kQS) & 1);
+        for (int ii = max(0, kv_issued - 2); ii < kv_issued; ++ii) mbar_wait_drain(&kv_full[ii & 1], (ii >> 1) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1 || warp >= 10) {
+    // ------------------------------------------------------------------ MMA issuers
+    // One thread issues a tcgen05.mma at most every ~50 cycles (a commit costs about as much),
+    // about the execution time of an N = 64 product, so the products are spread over three warps:
+    //   warp 1   S^T, dP^T of tile g (S^T / dP^T buffer g % 2 is free once dV, dK of tile g - 2
+    //            have read W^T / G^T from it)
+    //   warp 10  dV, dK of tile g (after the pointwise group has written W^T / G^T)
+    //   warp 11  dQ of tile g (after the pointwise group has written G to shared memory)
+    if (elect_one()) {
+      constexpr uint32_t idSdP = idesc_f16(1, 0, 0, kBM, kBN);  // N = 64 queries, M = 128 keys
+      constexpr uint32_t idAcc = idesc_f16(1, 0, 1, kD, kBN);   // A TMEM, B MN-major, N = 64
+      constexpr uint32_t idDQ = idesc_f16(1, 1, 1, kD, kBM);    // A, B MN-major, M = 64, N = 64
+      const int role = warp == 1 ? 0 : warp - 9;
+      bool ok = true;
+      int k = 0, i = 0, g = 0;
+      BwdItem it;
+      for (; ok && bwd_next(p, k, it); ++k, ++i) {
+        const int kb = i & 1;
+        if (role == 0) ok = mbar_wait(&kv_full[kb], (i >> 1) & 1, wc, 22);
+        for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
+          const int sb = g & 1;
+          const int qs = g % kQS;
+          const bool first = t == 0, last = t == it.n_tiles - 1;
+          if (role == 0) {
+            ok = mbar_wait(&q_full[qs], (g / kQS) & 1, wc, 23);
+            if (ok) ok = mbar_wait(&o_full[qs], (g / kQS) & 1, wc, 28);
+            if (ok && g >= 2) ok = mbar_wait(&dvk_done[sb], ((g - 2) >> 1) & 1, wc, 24);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t dK = sdesc_sw128(smem_u32(smem + kSK + kb * 32768), 16, 1024);
+            const uint64_t dV = sdesc_sw128(smem_u32(smem + kSV + kb * 32768), 16, 1024);
+            const uint64_t dQ = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 16, 1024);
+            const uint64_t ddO = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements per step: 32 B along the row
+              mma_ss(tmem + kTS + sb * kBM, dK + kk * 2, dQ + kk * 2, idSdP, kk > 0);
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk)
+              mma_ss(tmem + kTdP + sb * kBM, dV + kk * 2, ddO + kk * 2, idSdP, kk > 0);
+            mma_commit(&sdp_full[sb]);
+            if (last) mma_commit(&kv_empty[kb]);  // V, and K as far as S^T is concerned
+          } else if (role == 1) {
+            ok = mbar_wait(&wg_full[sb], (g >> 1) & 1, wc, 25);
+            if (ok && first && i >= 1) ok = mbar_wait(acc_empty, (i - 1) & 1, wc, 27);
+            if (!ok) break;
+            tc_fence_after();
+            // MN-major Q / dO (N = head dim); a K step of 16 queries is 16 rows = 2048 B
+            const uint64_t dQmn = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 8192, 1024);
+            const uint64_t ddOmn = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 8192, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns
+              mma_ts(tmem + kTdV, tmem + kTS + sb * kBM + kk * 8, ddOmn + kk * 128, idAcc, (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+            for (int kk = 0; kk < kBM / 16; ++kk)
+              mma_ts(tmem + kTdK, tmem + kTdP + sb * kBM + kk * 8, dQmn + kk * 128, idAcc, (first && kk == 0) ? 0u : 1u);
+            mma_commit(&q_empty[qs]);
+            mma_commit(&dvk_done[sb]);
+            if (last) mma_commit(acc_full);
+          } else {
+            ok = mbar_wait(&wg_full[sb], (g >> 1) & 1, wc, 26);
+            if (ok && g >= 2) ok = mbar_wait(&dq_empty[sb], ((g - 2) >> 1) & 1, wc, 29);
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t dG = sdesc_sw128(smem_u32(smem + kSG + (g & 3) * 16384), 16384, 1024);
+            const uint64_t dKmn = sdesc_sw128(smem_u32(smem + kSK + kb * 32768), 16384, 1024);
+#pragma unroll
+            for (int kk = 0; kk < kBN / 16; ++kk)  // 16 keys per step: 2048 B of G and of K
+              mma_ss(tmem + kTdQ + sb * kD, dG + kk * 128, dKmn + kk * 128, idDQ, kk > 0);
+            mma_commit(&dq_full[sb]);
+            if (last) mma_commit(&kv_empty[kb]);  // K as far as dQ is concerned
+          }
+        }
+      }
+      if (!ok) {  // wait for this thread's products in flight before TMEM is released
+        mma_commit(drain + role);
+        mbar_wait_drain(drain + role, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ pointwise (key rows)
+    const int wg = (warp - 2) >> 2;
+    const int lg = warp & 3;
+    const int jr = lg * 32 + lane;  // key row within the tile == TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    int* docq = reinterpret_cast<int*>(smem + kSDoc) + (wg * 4 + lg) * kBM;
+    uint8_t* g_row0 = smem + kSG + jr * 128;
+    uint8_t* stg = smem + kSStg + lg * 8192 + wg * 4096;  // this warp's dQ staging (two 16 x 32 boxes)
+    const bool leader = elect_one();
+    bool ok = true;
+    // dQ partial of global query tile u (TMEM buffer wg; an M=64 accumulator keeps rows
+    // 16lg..16lg+15 in lanes 0..15 of this warp's quadrant) -> swizzled staging -> TMA
+    // reduce-add into the fp32 accumulator at row grow
+    auto drain_dq = [&](int u, int grow) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&dq_full[wg], (u >> 1) & 1, wc, 29))) return false;
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      tmem_ld32(lane_addr + kTdQ + wg * kD, r0);
+      tmem_ld32(lane_addr + kTdQ + wg * kD + 32, r1);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&dq_empty[wg]);
+      if (leader) bulk_wait_read<0>();  // the previous reduce from this staging buffer has read it
+      __syncwarp();
+      if (lane < 16) {
+        uint8_t* row0 = stg + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(row0 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(r0[4 * c]), __uint_as_float(r0[4 * c + 1]), __uint_as_float(r0[4 * c + 2]),
+                          __uint_as_float(r0[4 * c + 3]));
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(row0 + 2048 + ((c ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(r1[4 * c]), __uint_as_float(r1[4 * c + 1]), __uint_as_float(r1[4 * c + 2]),
+                          __uint_as_float(r1[4 * c + 3]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (leader) {
+        tma_reduce_add_2d(&tmDQ, stg, 0, grow + 16 * lg);
+        tma_reduce_add_2d(&tmDQ, stg + 2048, 32, grow + 16 * lg);
+        bulk_commit();
+      }
+      return true;
+    };
+    int g = 0, i = 0;
+    int prev_g = -1, prev_row = 0;
+    // per-item parameters (map, this key row's document id) come from global memory; those of
+    // the next item are requested before the current item's end-of-item work hides their latency
+    int k = 0;
+    BwdItem it_n;
+    bool have_n = bwd_next(p, k, it_n);
+    Map map_n{};
+    int doc_n = 0;
+    auto fetch = [&]() {
+      map_n = BwdMap<Map>::make(p, it_n.h);
+      if constexpr (kHasDoc) {
+        const int kr = it_n.n0 + jr;
+        doc_n = kr < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)kr * p.doc_s1] : -2;
+      }
+    };
+    if (have_n) fetch();
+    for (; ok && have_n; ++i) {
+      const BwdItem it = it_n;
+      const Map map = map_n;
+      const int doc_j = doc_n;
+      (void)doc_j;
+      const int64_t bh = (int64_t)it.b * p.H + it.h;
+      const int n0 = it.n0;
+      const int kj = n0 + jr;
+      float g1 = 0.f, g2 = 0.f;
+      for (int t = (wg - g) & 1; t < it.n_tiles && ok; t += 2) {
+        const int gg = g + t;  // gg % 2 == wg
+        const int sb = wg;
+        const int m0 = it.m_first + t * kBM;
+        if constexpr (kHasDoc) {
+#pragma unroll
+          for (int u = 0; u < kBM / 32; ++u) {
+            const int qi = m0 + u * 32 + lane;
+            docq[u * 32 + lane] = qi < p.T ? p.doc[(int64_t)it.b * p.doc_s0 + (int64_t)qi * p.doc_s1] : -1;
+          }
+          __syncwarp();
+        }
+        ok = __all_sync(0xffffffffu, mbar_wait(&vec_full[gg % kQS], (gg / kQS) & 1, wc, 32));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[sb], (gg >> 1) & 1, wc, 30));
+        if (!ok) break;
+        tc_fence_after();
+        const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
+                          (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
+                          (n0 + kBN <= p.T);
+        const float* dl = vdlz + (gg % kQS) * kBM;
+        const float* zi = vzinv + (gg % kQS) * kBM;
+        uint8_t* g_row = g_row0 + (gg & 3) * 16384;  // this group's two G buffers alternate
+        const uint32_t s_col = lane_addr + kTS + sb * kBM, p_col = lane_addr + kTdP + sb * kBM;
+        // Partial tiles: the raw score of every invalid pair is replaced by NaN before the map,
+        // which turns it into p = 0 and dL/draw = 0 (fmaxf returns its non-NaN operand and no
+        // other term of these maps touches raw), so one branch-free body serves every tile.
+        const int lo_q = p.causal ? kj - m0 : -kBM;  // causal: query column qx is valid iff qx >= kj - m0
+        const int hi_q = kj < p.T ? p.T - m0 : 0;    // queries below T; a padded key row has none
+        auto mask16 = [&](int sc, uint32_t (&rs)[16]) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int qx = sc * 16 + e;
+            bool v = (qx >= lo_q) & (qx < hi_q) & ((p.window <= 0) | ((m0 + qx) - kj < p.window));
+            if constexpr (kHasDoc) v = v & (docq[qx] == doc_j);
+            rs[e] = v ? rs[e] : 0x7FC00000u;
+          }
+        };
+        // one 16-query sub-chunk: W, G -> TMEM (over consumed columns), G -> smem
+        auto sub16 = [&](int sc, const uint32_t (&rs)[16], const uint32_t (&rd)[16]) {
+          float zc[16], dc[16];
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 z4 = reinterpret_cast<const float4*>(zi + sc * 16)[v4];
+            const float4 d4 = reinterpret_cast<const float4*>(dl + sc * 16)[v4];
+            zc[4 * v4] = z4.x; zc[4 * v4 + 1] = z4.y; zc[4 * v4 + 2] = z4.z; zc[4 * v4 + 3] = z4.w;
+            dc[4 * v4] = d4.x; dc[4 * v4 + 1] = d4.y; dc[4 * v4 + 2] = d4.z; dc[4 * v4 + 3] = d4.w;
+          }
+          uint32_t wpk[8], gpk[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float wv[2], gv[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const float raw = __uint_as_float(rs[e + u]);
+              wv[u] = map.prob(raw, true) * zc[e + u];
+              gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+            }
+            wpk[e / 2] = pack2<true>(wv[0], wv[1]);
+            gpk[e / 2] = pack2<true>(gv[0], gv[1]);
+          }
+          tmem_st8(s_col + sc * 8, wpk);
+          tmem_st8(p_col + sc * 8, gpk);
+          // G (MN-major A operand of dQ): key row jr holds 64 queries = 128 B, 16-byte chunks swizzled
+          *reinterpret_cast<uint4*>(g_row + (((2 * sc) ^ (jr & 7)) << 4)) = make_uint4(gpk[0], gpk[1], gpk[2], gpk[3]);
+          *reinterpret_cast<uint4*>(g_row + (((2 * sc + 1) ^ (jr & 7)) << 4)) = make_uint4(gpk[4], gpk[5], gpk[6], gpk[7]);
+        };
+        {
+          // software pipeline: the TMEM loads of sub-chunk s+1 are in flight while s is computed
+          uint32_t sA[16], dA[16], sB[16], dB[16];
+          tmem_ld16(s_col, sA);
+          tmem_ld16(p_col, dA);
+          tmem_wait_ld();
+#pragma unroll
+          for (int sc = 0; sc < kBM / 16; sc += 2) {
+            tmem_ld16(s_col + (sc + 1) * 16, sB);
+            tmem_ld16(p_col + (sc + 1) * 16, dB);
+            if (!full) mask16(sc, sA);
+            sub16(sc, sA, dA);
+            tmem_wait_ld();
+            if (sc + 2 < kBM / 16) {
+              tmem_ld16(s_col + (sc + 2) * 16, sA);
+              tmem_ld16(p_col + (sc + 2) * 16, dA);
+            }
+            if (!full) mask16(sc + 1, sB);
+            sub16(sc + 1, sB, dB);
+            tmem_wait_ld();
+          }
+        }
+        tmem_wait_st();
+        fence_proxy_async_smem();  // G written by the generic proxy, read by the tensor core
+        tc_fence_before();
+        mbar_arrive(&wg_full[sb]);
+        // Drain the dQ partial of this group's previous tile now, after this tile's work is
+        // handed over: its product finished while this tile was computed, so the group does not
+        // wait for it.  (This tile's G buffer was last read by tile gg - 4, drained by then.)
+        if (prev_g >= 0) {
+          ok = drain_dq(prev_g, prev_row);
+          if (!ok) break;
+        }
+        prev_g = gg;
+        prev_row = (int)(bh * p.Tpad + m0);
+      }
+      if (!ok) break;
+      ++k;
+      have_n = bwd_next(p, k, it_n);
+      if (have_n) fetch();
+      // ---- end of the item: dK / dV rows (group 0 stores dV, group 1 stores dK), partials
+      ok = __all_sync(0xffffffffu, mbar_wait(acc_full, i & 1, wc, 31));
+      if (!ok) break;
+      tc_fence_after();
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK), r0);
+        tmem_ld32(lane_addr + (wg == 0 ? kTdV : kTdK) + 32, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(acc_empty);
+        // this warp's 32 rows -> its dQ staging buffer (128-byte swizzle) -> one TMA tensor store
+        // (a thread-per-row store would touch 32 rows per instruction)
+        if (leader) bulk_wait_read<0>();  // the staging buffer's previous reduce has read it
+        __syncwarp();
+        uint8_t* row = stg + lane * 128;
+        uint32_t w[32];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          w[e] = pack2<true>(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]));
+          w[16 + e] = pack2<true>(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]));
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(row + ((c ^ (lane & 7)) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (leader) {
+          tma_store_bhtd(wg == 0 ? &tmdV : &tmdK, stg, p.map3, 0, n0 + 32 * lg, it.h, it.b, p.H);
+          bulk_commit();
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        g1 += __shfl_xor_sync(0xffffffffu, g1, o);
+        g2 += __shfl_xor_sync(0xffffffffu, g2, o);
+      }
+      if (lane == 0) {
+        float* part = p.partials + ((bh * p.n_kv + it.kt) * 8 + (wg * 4 + lg)) * 2;
+        part[0] = g1;
+        part[1] = g2;
+      }
+      g += it.n_tiles;
+    }
+    if (ok && prev_g >= 0) ok = drain_dq(prev_g, prev_row);
+    if (leader) bulk_wait<0>();  // every reduce has finished reading shared memory
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Pre / post passes
+// ---------------------------------------------------------------------------------------------
+struct AuxParams {
+  int B, H, T, Tpad, D;
+  float eps;
+  const float* scale;
+  float* prep_part;  // [BH][Tpad / 64]: sum_i eps delta_i / Z_i over 64-row chunks
+  int purified;
+  const void* out;
+  int64_t o_s0, o_s1, o_s2, o_s3;
+  int out_f32;
+  const __nv_bfloat16* dout;
+  int64_t do_s0, do_s1, do_s2, do_s3;
+  const float* z;
+  float* dlz;
+  float* zinv;
+  float* dq_acc;
+  __nv_bfloat16* dq;
+  int64_t dq_s0, dq_s1, dq_s2;
+  const float* partials;
+  int n_kv;
+  float* dscale;
+  float* dtau;
+  int scale_per_head, tau_per_head;
+};
+
+// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id),
+// a zeroed dQ accumulator chunk, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
+// dscale / d gamma).  Eight lanes share a row (8 elements = 16 bytes of bf16 each), so a warp
+// reads four 128-byte rows per load instruction.
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
+  const int chunk = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane >> 3, part = lane & 7;  // row within the group of 4, 8-element slice
+  const int64_t bh = (int64_t)b * a.H + h;
+  __shared__ float csum_w[8];
+  float csum = 0.f;
+#pragma unroll
+  for (int r4 = 0; r4 < 2; ++r4) {
+    const int i = chunk * 64 + warp * 8 + r4 * 4 + sub;
+    const int64_t row = bh * a.Tpad + i;
+    float s = 0.f;
+    if (i < a.T) {
+      const int d0 = part * 8;
+      const __nv_bfloat16* dop = a.dout + (int64_t)b * a.do_s0 + (int64_t)h * a.do_s1 + (int64_t)i * a.do_s2 + d0;
+      const uint4 dv = *reinterpret_cast<const uint4*>(dop);
+      float o[8];
+      const int64_t oo = (int64_t)b * a.o_s0 + (int64_t)h * a.o_s1 + (int64_t)i * a.o_s2 + d0;
+      if (a.out_f32) {
+        const float4 x = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[0];
+        const float4 y = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.out) + oo)[1];
+        o[0] = x.x; o[1] = x.y; o[2] = x.z; o[3] = x.w; o[4] = y.x; o[5] = y.y; o[6] = y.z; o[7] = y.w;
+      } else {
+        const uint4 ov = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.out) + oo);
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          o[2 * x] = sm100::bf16_lo(ow[x]);
+          o[2 * x + 1] = sm100::bf16_hi(ow[x]);
+        }
+      }
+      const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+      for (int x = 0; x < 4; ++x) s += o[2 * x] * sm100::bf16_lo(dw[x]) + o[2 * x + 1] * sm100::bf16_hi(dw[x]);
+    }
+#pragma unroll
+    for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (part == 0) {
+      const float zi = i < a.T ? 1.f / a.z[bh * a.T + i] : 0.f;
+      a.dlz[row] = s * zi;
+      a.zinv[row] = zi;
+      csum += a.eps * s * zi;
+    }
+  }
+  // zero this chunk's 64 accumulator rows (64 x 64 fp32 = 16 KB, one float4 per thread x 4)
+  float4* acc = reinterpret_cast<float4*>(a.dq_acc + (bh * a.Tpad + chunk * 64) * a.D);
+#pragma unroll
+  for (int x = 0; x < 4; ++x) acc[x * 256 + threadIdx.x] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, off);
+  if (lane == 0) csum_w[warp] = csum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += csum_w[w];
+    a.prep_part[bh * (a.Tpad / 64) + chunk] = t;
+  }
+}
+
+// dQ accumulator -> bf16 (one thread per 8 elements)
+__global__ void __launch_bounds__(256) bwd_post_kernel(const AuxParams a) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_row = a.D / 8;
+  const int64_t rows = (int64_t)a.B * a.H * a.T;
+  if (idx >= rows * per_row) return;
+  const int c8 = (int)(idx % per_row);
+  const int64_t r = idx / per_row;
+  const int i = (int)(r % a.T);
+  const int64_t bh = r / a.T;
+  const int h = (int)(bh % a.H), b = (int)(bh / a.H);
+  const float4* src = reinterpret_cast<const float4*>(a.dq_acc + ((bh * a.Tpad + i) * a.D + c8 * 8));
+  const float4 x = src[0], y = src[1];
+  uint4 o;
+  o.x = sm100::pack2<true>(x.x, x.y);
+  o.y = sm100::pack2<true>(x.z, x.w);
+  o.z = sm100::pack2<true>(y.x, y.y);
+  o.w = sm100::pack2<true>(y.z, y.w);
+  *reinterpret_cast<uint4*>(a.dq + (int64_t)b * a.dq_s0 + (int64_t)h * a.dq_s1 + (int64_t)i * a.dq_s2 + c8 * 8) = o;
+}
+
+// Fixed-order sums into dscale / dtau (deterministic; replaces atomics, flash_born.py:319-322):
+//   plain     dscale_h = (2 / scale_h) sum_{b,i} eps delta_i / Z_i
+//   purified  dgamma_h = (4 / gamma_h) (sum_{b,i} eps delta_i / Z_i - sum eps_base b^2 dP),
+//             dtau_h   = sum -4 u^3 dP gamma        (the last two from the main kernel's partials)
+// One block per head: each thread sums a fixed strided subset, then a fixed-shape tree; block 0
+// also folds the heads together for shared (scalar) parameters after a second pass.
+__global__ void __launch_bounds__(256) bwd_param_kernel(const AuxParams a, float* head_terms) {
+  const int h = blockIdx.x;
+  const int nc = a.Tpad / 64;
+  __shared__ float r1[256], r2[256], rp[256];
+  float tp = 0.f, t1 = 0.f, t2 = 0.f;
+  for (int b = 0; b < a.B; ++b) {
+    const int64_t bhh = (int64_t)b * a.H + h;
+    for (int t = threadIdx.x; t < nc; t += 256) tp += a.prep_part[bhh * nc + t];
+    if (a.purified) {
+      const float* part = a.partials + bhh * a.n_kv * 16;
+      for (int t = threadIdx.x; t < a.n_kv * 8; t += 256) {
+        t1 += part[2 * t];
+        t2 += part[2 * t + 1];
+      }
+    }
+  }
+  rp[threadIdx.x] = tp;
+  r1[threadIdx.x] = t1;
+  r2[threadIdx.x] = t2;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      rp[threadIdx.x] += rp[threadIdx.x + w];
+      r1[threadIdx.x] += r1[threadIdx.x + w];
+      r2[threadIdx.x] += r2[threadIdx.x + w];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float sc = a.scale[a.scale_per_head ? h : 0];
+    const float d1 = a.purified ? (4.f / sc) * (rp[0] - r1[0]) : (2.f / sc) * rp[0];
+    const float d2 = r2[0];
+    if (a.scale_per_head) a.dscale[h] += d1;
+    if (a.dtau != nullptr && a.tau_per_head) a.dtau[h] += d2;
+    head_terms[2 * h] = d1;
+    head_terms[2 * h + 1] = d2;
+  }
+}
+
+// shared (scalar) scale / tau: the per-head terms added in head order
+__global__ void bwd_param_shared_kernel(const AuxParams a, const float* head_terms) {
+  float s1 = 0.f, s2 = 0.f;
+  for (int hh = 0; hh < a.H; ++hh) {
+    s1 += head_terms[2 * hh];
+    s2 += head_terms[2 * hh + 1];
+  }
+  if (!a.scale_per_head) a.dscale[0] += s1;
+  if (a.dtau != nullptr && !a.tau_per_head) a.dtau[0] += s2;
+}
+
+struct WsLayout {
+  size_t dlz, zinv, dq_acc, partials, prep_part, head_terms, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+WsLayout ws_layout(const Problem& p) {
+  const int Tpad = (p.T + kBM - 1) / kBM * kBM;
+  const size_t BH = (size_t)p.B * p.H;
+  const int n_kv = (p.T + kBN - 1) / kBN;
+  WsLayout w;
+  w.dlz = 0;
+  w.zinv = align256(w.dlz + BH * Tpad * 4);
+  w.dq_acc = align256(w.zinv + BH * Tpad * 4);
+  w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
+  w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
+  w.head_terms = align256(w.prep_part + BH * (Tpad / 64) * 4);
+  w.total = align256(w.head_terms + (size_t)p.H * 2 * 4);
+  return w;
+}
+
+int bwd_num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n = v;
+    else
+      n = 148;
+  }
+  return n;
+}
+
+bool rows16(const Tensor4& t) {  // 16-byte vector row stores of bf16 rows
+  if ((reinterpret_cast<uintptr_t>(t.ptr) & 15) != 0 || t.s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t.s[i] % 8 != 0) return false;
+  return true;
+}
+
+template <class Map, bool kHasDoc>
+int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp, const CUtensorMap& mk, const CUtensorMap& mv,
+                const CUtensorMap& mq, const CUtensorMap& mdo, const CUtensorMap& mdq, const CUtensorMap& mdk,
+                const CUtensorMap& mdv) {
+  auto kernel = tc_bwd_kernel<Map, kHasDoc>;
+  const uint32_t smem = kSmemBytes + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  dim3 grid(std::min(bp.n_items, bwd_num_sms()));
+  kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, mdq, mdk, mdv, bp);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  return FB_OK;
+}
+
+}  // namespace
+
+bool tc_bwd64_supported(const Problem& p) {
+  if (p.dtype != FB_BF16 || p.D != kD) return false;
+  if (!tma_ok(p.dk) || !tma_ok(p.dv)) return false;  // dK / dV rows leave through TMA stores
+  if (p.out_dtype != FB_BF16 && p.out_dtype != FB_F32) return false;
+  if (!tma_ok(p.q) || !tma_ok(p.k) || !tma_ok(p.v) || !tma_ok(p.dout)) return false;
+  if (!rows16(p.dq) || !rows16(p.dk) || !rows16(p.dv)) return false;
+  // the pre-pass reads O rows as 16-byte vectors
+  const int oelt = p.out_dtype == FB_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(p.o.ptr) & 15) != 0 || p.o.s[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((p.o.s[i] * oelt) % 16 != 0) return false;
+  return true;
+}
+
+size_t tc_bwd64_workspace(const Problem& p) { return ws_layout(p).total; }
+
+int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
+  if (!get_encoder()) return FB_ERR_NO_DEVICE;
+  CUtensorMap mk, mv, mq, mdo;
+  const bool map3 = bh_mergeable(pr.q, pr.H) && bh_mergeable(pr.k, pr.H) && bh_mergeable(pr.v, pr.H) &&
+                    bh_mergeable(pr.dout, pr.H) && bh_mergeable(pr.dk, pr.H) && bh_mergeable(pr.dv, pr.H);
+  CUtensorMap mdk, mdv;  // stores of 32 dK / dV rows per warp
+  if (!encode_bhtd(&mk, pr.k, pr.B, pr.H, pr.T, pr.D, kBN, map3) ||
+      !encode_bhtd(&mv, pr.v, pr.B, pr.H, pr.T, pr.D, kBN, map3) ||
+      !encode_bhtd(&mq, pr.q, pr.B, pr.H, pr.T, pr.D, kBM, map3) ||
+      !encode_bhtd(&mdo, pr.dout, pr.B, pr.H, pr.T, pr.D, kBM, map3) ||
+      !encode_bhtd(&mdk, pr.dk, pr.B, pr.H, pr.T, pr.D, 32, map3) ||
+      !encode_bhtd(&mdv, pr.dv, pr.B, pr.H, pr.T, pr.D, 32, map3))
+    return FB_ERR_ALIGN;
+  const WsLayout w = ws_layout(pr);
+  char* ws = static_cast<char*>(pr.ws);
+  const int Tpad = (pr.T + kBM - 1) / kBM * kBM;
+  const int n_kv = (pr.T + kBN - 1) / kBN;
+
+  AuxParams a{};
+  a.B = pr.B; a.H = pr.H; a.T = pr.T; a.Tpad = Tpad; a.D = pr.D;
+  a.eps = pr.eps;
+  a.scale = pr.scale;
+  a.prep_part = reinterpret_cast<float*>(ws + w.prep_part);
+  a.purified = pr.purified;
+  a.out = pr.o.ptr;
+  a.o_s0 = pr.o.s[0]; a.o_s1 = pr.o.s[1]; a.o_s2 = pr.o.s[2]; a.o_s3 = pr.o.s[3];
+  a.out_f32 = pr.out_dtype == FB_F32;
+  a.dout = static_cast<const __nv_bfloat16*>(pr.dout.ptr);
+  a.do_s0 = pr.dout.s[0]; a.do_s1 = pr.dout.s[1]; a.do_s2 = pr.dout.s[2]; a.do_s3 = pr.dout.s[3];
+  a.z = pr.z;
+  a.dlz = reinterpret_cast<float*>(ws + w.dlz);
+  a.zinv = reinterpret_cast<float*>(ws + w.zinv);
+  a.dq_acc = reinterpret_cast<float*>(ws + w.dq_acc);
+  a.dq = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dq.ptr));
+  a.dq_s0 = pr.dq.s[0]; a.dq_s1 = pr.dq.s[1]; a.dq_s2 = pr.dq.s[2];
+  a.partials = reinterpret_cast<float*>(ws + w.partials);
+  a.n_kv = n_kv;
+  a.dscale = pr.dscale;
+  a.dtau = pr.purified ? pr.dtau : nullptr;
+  a.scale_per_head = pr.scale_per_head;
+  a.tau_per_head = pr.tau_per_head;
+
+  BwdParams bp{};
+  bp.B = pr.B; bp.H = pr.H; bp.T = pr.T; bp.Tpad = Tpad;
+  bp.causal = pr.causal; bp.window = pr.window; bp.eps_base = pr.eps_base;
+  bp.scale = pr.scale; bp.scale_per_head = pr.scale_per_head;
+  bp.tau = pr.tau; bp.tau_per_head = pr.tau_per_head;
+  bp.doc = pr.doc; bp.doc_s0 = pr.doc_s[0]; bp.doc_s1 = pr.doc_s[1];
+  bp.dk = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dk.ptr));
+  bp.dk_s0 = pr.dk.s[0]; bp.dk_s1 = pr.dk.s[1]; bp.dk_s2 = pr.dk.s[2];
+  bp.dv = static_cast<__nv_bfloat16*>(const_cast<void*>(pr.dv.ptr));
+  bp.dv_s0 = pr.dv.s[0]; bp.dv_s1 = pr.dv.s[1]; bp.dv_s2 = pr.dv.s[2];
+  bp.dlz = a.dlz; bp.zinv = a.zinv; bp.dq_acc = a.dq_acc;
+  bp.partials = reinterpret_cast<float*>(ws + w.partials);
+  bp.n_kv = n_kv;
+  bp.n_items = n_kv * pr.B * pr.H;
+  bp.status = pr.status;
+  bp.map3 = map3;
+
+  CUtensorMap mdq;
+  if (!encode_rows_f32(&mdq, a.dq_acc, (int64_t)pr.B * pr.H * Tpad)) return FB_ERR_ALIGN;
+  bwd_prep_kernel<<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  int rc;
+  if (pr.purified)
+    rc = pr.doc ? launch_main<PurifiedMapTC, true>(pr, s, bp, mk, mv, mq, mdo, mdq, mdk, mdv)
+                : launch_main<PurifiedMapTC, false>(pr, s, bp, mk, mv, mq, mdo, mdq, mdk, mdv);
+  else
+    rc = pr.doc ? launch_main<PlainMapNoParam, true>(pr, s, bp, mk, mv, mq, mdo, mdq, mdk, mdv)
+                : launch_main<PlainMapNoParam, false>(pr, s, bp, mk, mv, mq, mdo, mdq, mdk, mdv);
+  if (rc != FB_OK) return rc;
+  const int64_t post_threads = (int64_t)pr.B * pr.H * pr.T * (pr.D / 8);
+  bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
+  float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
+  bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
+  int n = 4;
+  if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
+    bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
+    ++n;
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
+  *launches = n;
+  return FB_OK;
+}
+
+}  // namespace fb

@@ -120,7 +120,10 @@ def _fill_common(a: _lib.FbAttnArgs, q, k, v, out, z, scale_flat, tau_flat, doc,
     a.eps = float(eps)
     a.eps_base = float(eps_base)
     a.path = _PATH_CODE[_forced_path]
-    a.deterministic = 1
+    # torch.use_deterministic_algorithms(True) asks for a backward without floating-point atomics
+    # (the two-kernel tensor-core backward, or the general path); otherwise d=64 uses the fused
+    # tensor-core backward, whose dQ reduce-adds may sum in a different order from run to run
+    a.deterministic = int(torch.are_deterministic_algorithms_enabled())
     a.q, a.q_stride = _ptr(q), _strides(q)
     a.k, a.k_stride = _ptr(k), _strides(k)
     a.v, a.v_stride = _ptr(v), _strides(v)

@@ -47,15 +47,20 @@ def lowp_gate(x, r, name="", tol=LOWP_REL, floor=1e-30) -> None:
 
 
 def run_cuda(kind, q, k, v, do, scale, tau=None, eps_base=0.05, is_causal=True, eps=None, window_size=0,
-             doc_ids=None, dtype=torch.float32, path="auto", device="cuda"):
-    """Run the CUDA op fwd+bwd; return dict of float64 numpy arrays (out, dq, dk, dv, dscale[, dtau])."""
+             doc_ids=None, dtype=torch.float32, path="auto", device="cuda", deterministic=False):
+    """Run the CUDA op fwd+bwd; return dict of float64 numpy arrays (out, dq, dk, dv, dscale[, dtau]).
+
+    deterministic=True runs under torch.use_deterministic_algorithms(True), which selects the
+    backward without floating-point atomics."""
     qt, kt, vt = (torch.as_tensor(np.asarray(x), dtype=torch.float32).to(device=device, dtype=dtype)
                   .requires_grad_(True) for x in (q, k, v))
     dot = torch.as_tensor(np.asarray(do), dtype=torch.float32).to(device=device, dtype=dtype)
     sc = torch.as_tensor(np.asarray(scale, dtype=np.float32), device=device).requires_grad_(True)
     doc = None if doc_ids is None else torch.as_tensor(np.asarray(doc_ids), device=device)
     prev = fbm.get_kernel_path()
+    prev_det = torch.are_deterministic_algorithms_enabled()
     fbm.set_kernel_path(path)
+    torch.use_deterministic_algorithms(deterministic)
     try:
         if kind == "plain":
             out = flash_born_attention(qt, kt, vt, sc, is_causal=is_causal, eps=1e-12 if eps is None else eps,
@@ -70,6 +75,7 @@ def run_cuda(kind, q, k, v, do, scale, tau=None, eps_base=0.05, is_causal=True, 
         torch.cuda.synchronize()
     finally:
         fbm.set_kernel_path(prev)
+        torch.use_deterministic_algorithms(prev_det)
     res = {"out": out, "dq": qt.grad, "dk": kt.grad, "dv": vt.grad, "dscale": sc.grad}
     if ta is not None:
         res["dtau"] = ta.grad

@@ -117,13 +117,17 @@ BWD_CASES = CASES + [
 ]
 
 
+@pytest.mark.parametrize("deterministic", [False, True], ids=["fused", "deterministic"])
 @pytest.mark.parametrize("purified", [False, True])
 @pytest.mark.parametrize("case", BWD_CASES, ids=[str(c) for c in BWD_CASES])
-def test_tc_backward_matches_oracle(case, purified):
-    """Forward and backward both forced onto the tcgen05 kernels (d=64 and d=128), against the oracle."""
+def test_tc_backward_matches_oracle(case, purified, deterministic):
+    """Forward and backward both forced onto the tcgen05 kernels, against the oracle: d=64 through
+    the fused backward and (deterministic mode) the two-kernel one; d=128 always takes the latter."""
     from parity_util import check_all, run_cuda, run_oracle
 
     B, H, T, D, causal, window, doc_mean = case
+    if deterministic and D != 64:
+        pytest.skip("d=128 always uses the two-kernel backward")
     rng = np.random.default_rng(B * 11 + T + D)
     q, k, v, do = (rng.standard_normal((B, H, T, D)) for _ in range(4))
     if purified:
@@ -144,7 +148,21 @@ def test_tc_backward_matches_oracle(case, purified):
     if purified:
         kw["tau"] = np.linspace(0.02, 0.08, H).astype(np.float32)
     got = run_cuda("purified" if purified else "plain", q, k, v, do, scale, dtype=torch.bfloat16, path="tcgen05",
-                   **kw)
+                   deterministic=deterministic, **kw)
     assert fbm.device_status() == (0, 0)
     ref = run_oracle("purified" if purified else "plain", q, k, v, do, scale, **kw)
     check_all(got, ref, lowp=True)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_tc_backward_deterministic_mode_is_bitwise_repeatable(D):
+    """Under torch.use_deterministic_algorithms(True) two backward runs give identical bits."""
+    from parity_util import run_cuda
+
+    rng = np.random.default_rng(5)
+    q, k, v, do = (round_to(rng.standard_normal((2, 3, 700, D)), torch.bfloat16) for _ in range(4))
+    scale = np.full(3, 0.4, np.float32)
+    a = run_cuda("plain", q, k, v, do, scale, dtype=torch.bfloat16, path="tcgen05", deterministic=True)
+    b = run_cuda("plain", q, k, v, do, scale, dtype=torch.bfloat16, path="tcgen05", deterministic=True)
+    for name in ("dq", "dk", "dv", "dscale"):
+        assert np.array_equal(a[name], b[name]), name
