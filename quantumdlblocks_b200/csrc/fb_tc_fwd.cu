@@ -386,23 +386,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         // c < lg, entirely masked for c > lg, and valid for column e <= lane when c == lg
         const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 == it.m0;
         if (full) {
-          // 64 columns per round, both loads in flight before one wait
-#pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {
-            uint32_t r0[32], r1[32];
-            tmem_ld32(s_addr + hh * 64, r0);
-            tmem_ld32(s_addr + hh * 64 + 32, r1);
-            tmem_wait_ld();
-            uint32_t w0[16], w1[16];
+          // four 32-column chunks, software pipelined: the TMEM load of chunk c+1 is in flight
+          // while chunk c is turned into P (the loads would otherwise expose their latency)
+          uint32_t ra[32], rb[32];
+          auto chunk = [&](int c, const uint32_t (&r)[32]) {
+            uint32_t w[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              w0[e / 2] = pack2<true>(map.prob(__uint_as_float(r0[e]), true), map.prob(__uint_as_float(r0[e + 1]), true));
-              w1[e / 2] = pack2<true>(map.prob(__uint_as_float(r1[e]), true), map.prob(__uint_as_float(r1[e + 1]), true));
-              if constexpr (!Cfg::kTcZ)
-                zsum += (bf16_lo(w0[e / 2]) + bf16_hi(w0[e / 2])) + (bf16_lo(w1[e / 2]) + bf16_hi(w1[e / 2]));
+              w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), true), map.prob(__uint_as_float(r[e + 1]), true));
+              if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
             }
-            tmem_st16(p_addr + hh * 32, w0);
-            tmem_st16(p_addr + hh * 32 + 16, w1);
+            tmem_st16(p_addr + c * 16, w);
+          };
+          tmem_ld32(s_addr, ra);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < kBN / 32; c += 2) {
+            tmem_ld32(s_addr + (c + 1) * 32, rb);
+            chunk(c, ra);
+            tmem_wait_ld();
+            if (c + 2 < kBN / 32) tmem_ld32(s_addr + (c + 2) * 32, ra);
+            chunk(c + 1, rb);
+            tmem_wait_ld();
           }
         } else if (diag) {
 #pragma unroll 1
