@@ -23,6 +23,7 @@ import argparse
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -45,6 +46,21 @@ WORKLOADS = {
     "c3": (1, 32, 16384, 128, True, "C3 B=1 H=32 N=16384 d=128 causal bf16, unit-norm*sqrt(d) Q/K"),
     "c4": (4, 16, 8192, 64, True, "C4 B=4 H=16 N=8192 d=64 doc-masked bf16 (geometric doc lengths, mean 512)"),
 }
+
+
+def profiled_traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary
+    (profiles/tc_{fwd,bwd}_kernel_c2.md, line 'traffic X MB per launch'); None when the summary
+    does not cover this workload."""
+    if workload != "c2":
+        return None
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", f"tc_{kernel}_kernel_c2.md")
+    try:
+        text = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic ([0-9.]+) MB per launch", text)
+    return float(m.group(1)) * 1e6 if m else None
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -329,10 +345,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     hq, hk, hv, hdo = (x.to(bf).pin_memory() for x in (q_cpu, k_cpu, v_cpu, do_cpu))
     h_out = [torch.empty_like(hq).pin_memory() for _ in range(4)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(e2e_steps):
+
+    def e2e_step():
         xq = hq.to(dev, non_blocking=True).requires_grad_(True)
         xk = hk.to(dev, non_blocking=True).requires_grad_(True)
         xv = hv.to(dev, non_blocking=True).requires_grad_(True)
@@ -340,6 +354,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         out, (gq, gk, gv, _) = step(xq, xk, xv, xd)
         for dst, src in zip(h_out, (out, gq, gk, gv)):
             dst.copy_(src, non_blocking=True)
+
+    e2e_step()  # untimed: first use of these buffer sizes in the caching allocator
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
     e1.record()
     torch.cuda.synchronize()
     barrier()
@@ -393,7 +414,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                 peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])),
             "roofline": {"bound": "tensor", "kernel": f"{dominant} ({path_bwd if dominant == 'bwd' else path_fwd})",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                         "peak_source": f"bf16_tflops (burst) of {peak_src}", "traffic": None,
+                         "peak_source": f"bf16_tflops (burst) of {peak_src}",
+                         "traffic": profiled_traffic(args.workload, dominant),
+                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant "
+                                           "kernel, profiles/tc_*_kernel_c2.md (ncu capture of this build)",
                          "fwd_ms": t_fwd, "bwd_ms": t_bwd, "fwd_launches": n_fwd_launch,
                          "bwd_launches": n_bwd_launch,
                          "fwd_tflops": flops_fwd / (t_fwd / 1e3) / 1e12,

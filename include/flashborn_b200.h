@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define FB_ABI_VERSION 1
+#define FB_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define FB_API __attribute__((visibility("default")))
@@ -110,6 +110,8 @@ typedef struct fb_attn_args {
   float* dscale; /* accumulated, scale_numel elements */
   float* dtau;   /* accumulated, tau_numel elements (purified) */
 
+  /* Backward: fb_bwd_workspace_size() bytes.  Forward: fb_fwd_workspace_size() bytes, which is
+   * non-zero only with doc_ids on the tensor-core path (document spans used to skip tiles). */
   void* workspace; size_t workspace_bytes;
 } fb_attn_args;
 
@@ -143,6 +145,12 @@ FB_API int fb_born_bwd_static_scratch(const fb_attn_args* args, void* stream);
  * A non-NULL tau marks purified arguments here and in fb_select_path.
  * The reference allocates the equivalent scratch implicitly (delta is recomputed per tile). */
 FB_API size_t fb_bwd_workspace_size(const fb_attn_args* args);
+
+/* Bytes of device workspace the forward needs for these arguments: 0 without doc_ids; with them,
+ * room for the per-64-row-block document spans that let the tensor-core kernels skip tiles with
+ * no same-document pair.  ABI version 2.  No counterpart in the reference (its forward visits
+ * every causal tile and masks, flash_born.py:169-178). */
+FB_API size_t fb_fwd_workspace_size(const fb_attn_args* args);
 
 /* Which path fb_*_fwd / fb_*_bwd would take for these arguments: FB_PATH_TCGEN05 or
  * FB_PATH_GENERAL, or a negative FB_ERR_* if the arguments are invalid. `backward` selects

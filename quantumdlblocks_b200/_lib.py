@@ -68,6 +68,7 @@ SIGNATURES = {
     "fb_purified_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_purified_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_bwd_workspace_size": (ctypes.c_size_t, [_PARGS]),
+    "fb_fwd_workspace_size": (ctypes.c_size_t, [_PARGS]),
     "fb_select_path": (ctypes.c_int, [_PARGS, ctypes.c_int]),
     "fb_last_launch_count": (ctypes.c_int, []),
     "fb_device_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]),

@@ -91,6 +91,7 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, b
   p->q = t4(a->q, a->q_stride); p->k = t4(a->k, a->k_stride); p->v = t4(a->v, a->v_stride);
   p->o = t4(a->out, a->out_stride);
   p->z = a->z;
+  p->ws = a->workspace; p->ws_bytes = a->workspace_bytes;  // forward: document ranges only
   if (!empty && !query_only) {
     int rc;
     if ((rc = check_tensor(a->q, a->q_stride)) || (rc = check_tensor(a->k, a->k_stride)) ||
@@ -127,7 +128,8 @@ int choose_path(const fb_attn_args* a, const Problem& p, bool backward) {
   return tc ? FB_PATH_TCGEN05 : FB_PATH_GENERAL;
 }
 
-size_t workspace_for(const Problem& p, int path) {
+size_t workspace_for(const Problem& p, int path, bool backward) {
+  if (!backward) return path == FB_PATH_TCGEN05 ? doc_ranges_bytes(p) : 0;  // forward: document ranges
   if (path != FB_PATH_TCGEN05) return general_bwd_workspace(p);
   return use_fused_bwd(p) ? tc_bwd64_workspace(p) : tc_bwd_workspace(p);
 }
@@ -142,8 +144,8 @@ int run(const fb_attn_args* a, void* stream, bool purified, bool backward) {
   }
   const int path = choose_path(a, p, backward);
   if (path < 0) return -path;
-  if (backward && p.ws_bytes < workspace_for(p, path)) return FB_ERR_WORKSPACE;
-  if (backward && p.ws == nullptr && workspace_for(p, path) > 0) return FB_ERR_WORKSPACE;
+  const size_t ws_need = workspace_for(p, path, backward);
+  if (p.ws_bytes < ws_need || (p.ws == nullptr && ws_need > 0)) return FB_ERR_WORKSPACE;
   p.status = status_ptr(&rc);
   if (rc != FB_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -182,7 +184,16 @@ size_t fb_bwd_workspace_size(const fb_attn_args* args) {
   if (fb::normalise(args, purified, true, &p, true) != FB_OK) return 0;
   const int path = fb::choose_path(args, p, true);
   if (path < 0) return 0;
-  return fb::workspace_for(p, path);
+  return fb::workspace_for(p, path, true);
+}
+
+size_t fb_fwd_workspace_size(const fb_attn_args* args) {
+  fb::Problem p;
+  const bool purified = args != nullptr && args->tau != nullptr;
+  if (fb::normalise(args, purified, false, &p, true) != FB_OK) return 0;
+  const int path = fb::choose_path(args, p, false);
+  if (path < 0) return 0;
+  return fb::workspace_for(p, path, false);
 }
 
 int fb_select_path(const fb_attn_args* args, int backward) {
@@ -222,7 +233,7 @@ const char* fb_strerror(int status) {
     case FB_ERR_ARG: return "flashborn: invalid argument (null pointer, scale/tau length not 1 or H, negative window, bad path)";
     case FB_ERR_LAUNCH: return "flashborn: CUDA launch failed (see fb_last_cuda_error)";
     case FB_ERR_TIMEOUT: return "flashborn: a device-side pipeline wait exceeded its bound; the kernel stopped early and its outputs are invalid";
-    case FB_ERR_WORKSPACE: return "flashborn: backward workspace missing or smaller than fb_bwd_workspace_size()";
+    case FB_ERR_WORKSPACE: return "flashborn: workspace missing or smaller than fb_bwd_workspace_size() / fb_fwd_workspace_size()";
     case FB_ERR_NO_DEVICE: return "flashborn: no usable CUDA device";
     case FB_ERR_UNSUPPORTED: return "flashborn: the forced tcgen05 path does not support this configuration";
     case FB_ERR_SCRATCH_LIMIT: return "flashborn: this backward needs more scratch than the library's static array (FB_STATIC_SCRATCH_BYTES); call fb_born_bwd with a workspace instead";

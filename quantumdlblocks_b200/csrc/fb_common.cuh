@@ -147,6 +147,35 @@ struct PurifiedMapTC : PurifiedMap {
   }
 };
 
+// ------------------------------------------------------------------------------------------
+// Document-mask tile ranges (fb_docs.cu): per 64-row block, the span of blocks on the other side
+// that can share a document id with it (qr: key blocks of a query block; kr: query blocks of a
+// key block).  Tiles outside a span hold no valid pair and are skipped.
+// ------------------------------------------------------------------------------------------
+constexpr int kDocBlock = 64;
+__host__ __device__ inline int doc_blocks(int T) { return (T + kDocBlock - 1) / kDocBlock; }
+struct DocRanges {
+  const int2* qr;
+  const int2* kr;
+  int nblk;
+};
+
+// Narrows the other side's row range [lo, hi) of a tile whose own rows are [row0, row0 + rows) to
+// the blocks that can share a document with those rows; no-op without document ids (r == null).
+__device__ __forceinline__ void doc_narrow(const int2* r, int nblk, int b, int row0, int rows, int& lo, int& hi) {
+  if (r == nullptr) return;
+  const int x0 = row0 / kDocBlock;
+  const int x1 = min((row0 + rows - 1) / kDocBlock, nblk - 1);
+  int f = nblk, l = -1;
+  for (int x = x0; x <= x1; ++x) {
+    const int2 v = __ldg(&r[(int64_t)b * nblk + x]);
+    f = min(f, v.x);
+    l = max(l, v.y);
+  }
+  lo = max(lo, f * kDocBlock);
+  hi = min(hi, (l + 1) * kDocBlock);
+}
+
 __device__ __forceinline__ void set_status(int* status, int code, int site) {
   if (status != nullptr && atomicCAS(status, 0, code) == 0) status[1] = site;
 }
@@ -167,6 +196,9 @@ bool tc_bwd64_supported(const Problem& p);  // fused backward (fb_tc_bwd64.cu), 
 int tc_bwd64(const Problem& p, cudaStream_t s, int* launches);
 size_t tc_bwd64_workspace(const Problem& p);
 void record_cuda_error(cudaError_t e);
+// document-mask tile ranges (fb_docs.cu): bytes of workspace, and the two launches that fill it
+size_t doc_ranges_bytes(const Problem& p);
+int doc_ranges(const Problem& p, cudaStream_t s, void* ws, DocRanges* out);
 // TMA tensor maps (fb_tmap.cu)
 bool get_encoder();
 bool tma_ok(const Tensor4& t);

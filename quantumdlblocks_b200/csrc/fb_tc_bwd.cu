@@ -76,6 +76,9 @@ struct BwdParams {
   float* partials;     // [BH][n_kv][8 warps][2]
   int n_kv, n_items;   // key-major kernel: 128-key tiles per head, work items
   int n_mt, n_qitems;  // query-major kernel: 128-query tiles per head, work items
+  const int2* doc_qr;  // document spans of the query / key blocks (null without document ids)
+  const int2* doc_kr;
+  int nblk;
   int* status;
 };
 
@@ -140,6 +143,7 @@ __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int bh, int kt) 
   int lo = p.causal ? it.n0 : 0;
   int hi = p.T;
   if (p.window > 0) hi = min(p.T, it.n0 + 128 - 1 + p.window);
+  doc_narrow(p.doc_kr, p.nblk, it.b, it.n0, 128, lo, hi);  // queries that can share a document
   lo = (lo / 64) * 64;
   it.m_first = lo;
   it.n_tiles = hi > lo ? (hi - lo + 63) / 64 : 0;
@@ -618,6 +622,7 @@ __device__ __forceinline__ QItem q_item(const BwdParams& p, int idx) {
   int lo = 0, hi = p.T;
   if (p.causal) hi = min(p.T, it.m0 + 128);
   if (p.window > 0) lo = max(0, it.m0 - p.window + 1);
+  doc_narrow(p.doc_qr, p.nblk, it.b, it.m0, 128, lo, hi);  // keys that can share a document
   lo = (lo / 64) * 64;
   it.n_first = lo;
   it.n_count = hi > lo ? (hi - lo + 63) / 64 : 0;
@@ -1093,7 +1098,7 @@ __global__ void bwd_param_shared_kernel(const AuxParams a, const float* head_ter
 }
 
 struct WsLayout {
-  size_t zd, partials, prep_part, head_terms, total;
+  size_t zd, partials, prep_part, head_terms, docs, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -1109,7 +1114,8 @@ WsLayout ws_layout(const Problem& p) {
   w.partials = align256(w.zd + BH * Tpad * 8);
   w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
   w.head_terms = align256(w.prep_part + BH * (Tpad / 64) * 4);
-  w.total = align256(w.head_terms + (size_t)p.H * 2 * 4);
+  w.docs = align256(w.head_terms + (size_t)p.H * 2 * 4);
+  w.total = align256(w.docs + doc_ranges_bytes(p));
   return w;
 }
 
@@ -1239,6 +1245,12 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   bp.status = pr.status;
   bp.map3 = bh_mergeable(pr.q, pr.H) && bh_mergeable(pr.k, pr.H) && bh_mergeable(pr.v, pr.H) &&
             bh_mergeable(pr.dout, pr.H);
+  DocRanges dr;
+  const int drc = doc_ranges(pr, s, ws + w.docs, &dr);
+  if (drc != FB_OK) return drc;
+  bp.doc_qr = dr.qr;
+  bp.doc_kr = dr.kr;
+  bp.nblk = dr.nblk;
 
   if (pr.D == 64)
     bwd_prep_kernel<64><<<dim3(Tpad / 64, pr.H, pr.B), 256, 0, s>>>(a);
@@ -1254,7 +1266,7 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (rc != FB_OK) return rc;
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
   bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
-  int n = 4;
+  int n = 4 + (pr.doc != nullptr ? 2 : 0);
   if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
     bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
     ++n;

@@ -90,6 +90,8 @@ struct BwdParams {
   float* partials;     // [BH][n_kv][8 warps][2]
   int n_kv, n_items;
   int map3;            // tensor maps address (b, h) as one merged dimension
+  const int2* doc_kr;  // document spans of the key blocks (null without document ids)
+  int nblk;
   int* status;
 };
 
@@ -126,6 +128,7 @@ __device__ __forceinline__ BwdItem bwd_item(const BwdParams& p, int bh, int kt) 
   int lo = p.causal ? it.n0 : 0;
   int hi = p.T;
   if (p.window > 0) hi = min(p.T, it.n0 + kBN - 1 + p.window);
+  doc_narrow(p.doc_kr, p.nblk, it.b, it.n0, kBN, lo, hi);  // queries that can share a document
   lo = (lo / kBM) * kBM;
   it.m_first = lo;
   it.n_tiles = hi > lo ? (hi - lo + kBM - 1) / kBM : 0;
@@ -776,7 +779,7 @@ __global__ void bwd_param_shared_kernel(const AuxParams a, const float* head_ter
 }
 
 struct WsLayout {
-  size_t dlz, zinv, dq_acc, partials, prep_part, head_terms, total;
+  size_t dlz, zinv, dq_acc, partials, prep_part, head_terms, docs, total;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -792,7 +795,8 @@ WsLayout ws_layout(const Problem& p) {
   w.partials = align256(w.dq_acc + BH * Tpad * kD * 4);
   w.prep_part = align256(w.partials + BH * n_kv * 8 * 2 * 4);
   w.head_terms = align256(w.prep_part + BH * (Tpad / 64) * 4);
-  w.total = align256(w.head_terms + (size_t)p.H * 2 * 4);
+  w.docs = align256(w.head_terms + (size_t)p.H * 2 * 4);
+  w.total = align256(w.docs + doc_ranges_bytes(p));
   return w;
 }
 
@@ -906,6 +910,11 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   bp.n_items = n_kv * pr.B * pr.H;
   bp.status = pr.status;
   bp.map3 = map3;
+  DocRanges dr;
+  const int drc = doc_ranges(pr, s, ws + w.docs, &dr);
+  if (drc != FB_OK) return drc;
+  bp.doc_kr = dr.kr;
+  bp.nblk = dr.nblk;
 
   CUtensorMap mdq;
   if (!encode_rows_f32(&mdq, a.dq_acc, (int64_t)pr.B * pr.H * Tpad)) return FB_ERR_ALIGN;
@@ -924,7 +933,7 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
   bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
-  int n = 4;
+  int n = 4 + (pr.doc != nullptr ? 2 : 0);
   if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
     bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
     ++n;

@@ -94,6 +94,8 @@ struct FwdParams {
   int tau_per_head;
   const int32_t* doc;
   int64_t doc_s0, doc_s1;
+  const int2* doc_qr;  // document spans of the query blocks (null without document ids)
+  int nblk;
   void* out;
   int64_t o_s0, o_s1, o_s2;
   float* z;
@@ -114,7 +116,8 @@ struct Item {
   int b, h, m0, n_first, n_count;
 };
 
-// Work item idx: latest query tiles (the most keys under a causal mask) first, then (b, h).
+// Work item idx: latest query tiles (the most keys under a causal mask) first, then (b, h).  Its
+// key tiles span the causal / window range, narrowed to the documents of its rows.
 __device__ __forceinline__ Item item_at(const FwdParams& p, int idx) {
   const int bh_total = p.B * p.H;
   const int mt = p.n_mt - 1 - idx / bh_total;
@@ -126,6 +129,7 @@ __device__ __forceinline__ Item item_at(const FwdParams& p, int idx) {
   int lo = 0, hi = p.T;
   if (p.causal) hi = min(p.T, it.m0 + kBM);
   if (p.window > 0) lo = max(0, it.m0 - p.window + 1);
+  doc_narrow(p.doc_qr, p.nblk, it.b, it.m0, kBM, lo, hi);  // keys that can share a document
   lo = (lo / kBN) * kBN;
   it.n_first = lo;
   it.n_count = hi > lo ? (hi - lo + kBN - 1) / kBN : 0;
@@ -590,6 +594,11 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   fp.scale = pr.scale; fp.scale_per_head = pr.scale_per_head;
   fp.tau = pr.tau; fp.tau_per_head = pr.tau_per_head;
   fp.doc = pr.doc; fp.doc_s0 = pr.doc_s[0]; fp.doc_s1 = pr.doc_s[1];
+  DocRanges dr;
+  const int drc = doc_ranges(pr, s, pr.ws, &dr);  // workspace of doc_ranges_bytes(pr) bytes
+  if (drc != FB_OK) return drc;
+  fp.doc_qr = dr.qr;
+  fp.nblk = dr.nblk;
   fp.out = const_cast<void*>(pr.o.ptr);
   fp.o_s0 = pr.o.s[0]; fp.o_s1 = pr.o.s[1]; fp.o_s2 = pr.o.s[2];
   fp.z = pr.z;
@@ -599,7 +608,7 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
     rc = pr.purified ? fwd_doc<64, PurifiedMap>(pr, s, fp, mq, mk, mv) : fwd_doc<64, PlainMap>(pr, s, fp, mq, mk, mv);
   else
     rc = pr.purified ? fwd_doc<128, PurifiedMap>(pr, s, fp, mq, mk, mv) : fwd_doc<128, PlainMap>(pr, s, fp, mq, mk, mv);
-  if (rc == FB_OK) *launches = 1;
+  if (rc == FB_OK) *launches = 1 + (pr.doc != nullptr ? 2 : 0);
   return rc;
 }
 

@@ -164,6 +164,12 @@ def _born_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: torch.Te
     lib = _lib.load()
     a = _lib.FbAttnArgs()
     _fill_common(a, q, k, v, out, z, scale, tau, doc_ids, is_causal, eps, window_size, eps_base)
+    ws = None
+    if doc_ids is not None:  # document spans for tile skipping
+        ws_bytes = int(lib.fb_fwd_workspace_size(ctypes.byref(a)))
+        if ws_bytes:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+            a.workspace, a.workspace_bytes = _ptr(ws), ws_bytes
     with torch.cuda.device(q.device):
         fn = lib.fb_purified_born_fwd if purified else lib.fb_born_fwd
         _lib.check(fn(ctypes.byref(a), _stream_handle(q.device)), "flash-Born forward")
