@@ -249,6 +249,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     from quantumdlblocks_b200 import flash_born_attention
     from quantumdlblocks_b200.kernels import flash_born as fbm
+    from quantumdlblocks_b200.sharding import max_over_ranks
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -368,11 +369,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     h2d = 4 * hq.numel() * hq.element_size()
     d2h = 4 * hq.numel() * hq.element_size()
 
-    # max over ranks
-    times = torch.tensor([t_ms, e2e_ms, t_fwd, t_bwd], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_ms, e2e_ms, t_fwd, t_bwd = (float(x) for x in times.tolist())
+    # a job takes as long as its slowest rank
+    t_ms, e2e_ms, t_fwd, t_bwd = max_over_ranks([t_ms, e2e_ms, t_fwd, t_bwd], device=dev)
 
     peaks, peak_src = load_peaks()
     value = world * flops_step * args.steps / (t_ms / 1e3) / 1e12

@@ -6,15 +6,16 @@
 // runs; callers that ask for deterministic gradients get the two-kernel backward of fb_tc_bwd.cu,
 // which also serves head dim 128 (whose accumulators do not fit in TMEM next to dQ's).
 //
-// Three launches (all on the caller's stream):
+// Four launches (all on the caller's stream; two more compute the document spans when document
+// ids are given):
 //   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
 //                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
 //   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
 //                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
-//                        tiles that can hold valid
-//                        pairs and accumulates dK, dV in TMEM; dQ partials are reduced into the
-//                        fp32 accumulator with TMA tensor reduce-add.  The query-tile pipeline
-//                        runs on across items (K, V double-buffered per item)
+//                        tiles that can hold valid pairs and accumulates dK, dV in TMEM; dQ
+//                        partials are reduced into the fp32 accumulator with TMA tensor
+//                        reduce-add.  The query-tile pipeline runs on across items (K, V
+//                        double-buffered per item)
 //   3. bwd_post_kernel   dQ = accumulator -> input dtype
 //   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
 //                        sums and the main kernel's per-CTA partials
@@ -30,11 +31,18 @@
 //   dK  += G^T Q        same                              A=G^T (TMEM), B=Q (smem MN-major)
 //   dQ_t = G K          M=64 queries, N=64, K=128 keys    A=G (smem MN-major), B=K (smem MN-major)
 //
-// Warps (320 threads): 0 TMA producer, 1 TMEM owner + MMA issuer, 2-9 two pointwise warpgroups
-// (key rows; group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two
-// groups' latency chains interleave).  Before each tile a group drains the dQ partial of its
-// previous tile (TMEM -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator).  S^T/dP^T/dQ are double-buffered in TMEM so
-// the products of query tile t+1 overlap the pointwise work of tile t.
+// Warps (384 threads): 0 TMA producers (copies issued by one thread complete one after another,
+// about 0.3 us each, so lane 0 requests K / V and Q, lane 1 dO, lanes 2 and 3 the delta / Z and
+// 1 / Z vectors); 1 TMEM owner + issuer of S^T and dP^T; 2-9 two pointwise warpgroups (key rows;
+// group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two groups' latency
+// chains interleave); 10 issuer of dV and dK; 11 issuer of dQ.  One thread issues a tcgen05.mma
+// at most every ~50 cycles, about the execution time of an N = 64 product, so each product family
+// has its own issuing warp.  At the end of each tile a group drains that tile's dQ partial (TMEM
+// -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator); at the end of an item it
+// stores dK and dV (TMEM -> swizzled smem -> TMA tensor store).  S^T/dP^T/dQ are double-buffered
+// in TMEM so the products of query tile t+1 overlap the pointwise work of tile t.  Invalid pairs
+// take a NaN raw score, which the ReLU (fmaxf) turns into a = 0, so one branch-free pointwise body
+// serves diagonal, window, document and ragged tiles.
 //
 // TMEM columns: S^T[0..1] 0/64, dP^T[0..1] 128/192, dV 256, dK 320, dQ[0..1] 384/448.
 #include <cuda.h>

@@ -5,7 +5,7 @@
 // walks the key tiles (128 keys) that can hold valid pairs (causal / window tile skipping, as
 // flash_born.py:152-156).  The tile sequence is flattened across items, so the TMA ring, the
 // TMEM double buffers and the mbarrier phases run on from one item into the next and the
-// per-item set-up latency is hidden.  Warp-specialised pipeline (320 threads):
+// per-item set-up latency is hidden.  Warp-specialised pipeline (352 threads):
 //
 //   warp 0      TMA producers: copies issued by one thread complete one after another (about
 //               0.3 us each, whatever their size), so lane 0 requests Q of an item (double-
