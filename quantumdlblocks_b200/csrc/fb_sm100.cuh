@@ -98,6 +98,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// Time-bounded wait until a monotonic shared-memory counter (written by another thread of the
+// CTA with plain stores) reaches target.  Counters do not wrap as mbarrier phases do, so a waiter
+// that falls behind never mistakes a later phase for the one it wants.
+__device__ __forceinline__ bool wait_count(const volatile int* c, int target, const WaitCtx& w, int site) {
+  if (*c >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (*c < target) {
+    if ((++it & 15u) == 0) {
+      if (*w.abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *w.abort_flag = 1;
+        if (w.status != nullptr && atomicCAS(w.status, 0, FB_ERR_TIMEOUT) == 0) w.status[1] = site;
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // Time-bounded wait that ignores the abort flag: used on the abort path to let copies and MMAs
 // already in flight land before the CTA releases its shared and tensor memory.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {

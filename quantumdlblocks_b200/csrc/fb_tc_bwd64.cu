@@ -31,13 +31,13 @@
 //   dK  += G^T Q        same                              A=G^T (TMEM), B=Q (smem MN-major)
 //   dQ_t = G K          M=64 queries, N=64, K=128 keys    A=G (smem MN-major), B=K (smem MN-major)
 //
-// Warps (384 threads): 0 TMA producers (copies issued by one thread complete one after another,
+// Warps (448 threads): 0 TMA producers (copies issued by one thread complete one after another,
 // about 0.3 us each, so lane 0 requests K / V and Q, lane 1 dO, lanes 2 and 3 the delta / Z and
-// 1 / Z vectors); 1 TMEM owner + issuer of S^T and dP^T; 2-9 two pointwise warpgroups (key rows;
-// group g takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two groups' latency
-// chains interleave); 10 issuer of dV and dK; 11 issuer of dQ.  One thread issues a tcgen05.mma
-// at most every ~50 cycles, about the execution time of an N = 64 product, so each product family
-// has its own issuing warp.  At the end of each tile a group drains that tile's dQ partial (TMEM
+// 1 / Z vectors); 1 TMEM owner + issuer of S^T; 2-9 two pointwise warpgroups (key rows; group g
+// takes the query tiles t with t % 2 == g, i.e. TMEM buffer g, so the two groups' latency chains
+// interleave); 10 issuer of dV; 11 issuer of dQ; 12 issuer of dP^T; 13 issuer of dK.  One thread
+// issues a tcgen05.mma at most every ~50 cycles, about the execution time of an N = 64 product, so
+// each product has its own issuing warp.  At the end of each tile a group drains that tile's dQ partial (TMEM
 // -> swizzled smem -> TMA tensor reduce-add into the fp32 accumulator); at the end of an item it
 // stores dK and dV (TMEM -> swizzled smem -> TMA tensor store).  S^T/dP^T/dQ are double-buffered
 // in TMEM so the products of query tile t+1 overlap the pointwise work of tile t.  Invalid pairs
@@ -48,6 +48,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "fb_common.cuh"
 #include "fb_sm100.cuh"
@@ -60,7 +61,7 @@ using namespace sm100;
 constexpr int kBN = 128;  // keys per CTA
 constexpr int kBM = 64;   // queries per step
 constexpr int kD = 64;
-constexpr int kThreads = 384;  // 12 warps
+constexpr int kThreads = 448;  // 14 warps
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTS = 0, kTdP = 128, kTdV = 256, kTdK = 320, kTdQ = 384;
 
@@ -183,11 +184,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
                   const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmdK,
                   const __grid_constant__ CUtensorMap tmdV, const BwdParams p) {
+  // Plain map: the per-row vectors carry scale^2 (bwd_prep_kernel) and the pointwise body writes
+  // G / 2, which saves three multiplies per pair; dK and dQ are doubled where they are stored.
+  constexpr bool kFold = std::is_same<Map, PlainMapNoParam>::value;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSBar);
   uint64_t* kv_full = bars + 0;                // [2] per item parity
-  uint64_t* kv_empty = bars + 2;               // [2] (S^T / dP^T issuer and dQ issuer)
+  uint64_t* kv_empty = bars + 2;               // [2] (S^T, dP^T and dQ issuers)
   uint64_t* q_full = bars + 4;                 // [kQS] per query-tile stage: Q
   uint64_t* o_full = q_full + kQS;             // [kQS] dO
   uint64_t* vec_full = o_full + kQS;           // [kQS] delta / Z and 1 / Z (two copies)
@@ -199,10 +203,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_empty = dq_full + 2;            // [2]
   uint64_t* acc_full = dq_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
-  uint64_t* drain = acc_full + 2;              // [3] one per MMA-issuing warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 4);
-  static_assert((4 + 4 * kQS + 10 + 2 + 3 + 2) * 8 <= 512, "barrier area");
+  uint64_t* drain = acc_full + 2;              // [5] one per MMA-issuing warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(drain + 6);
+  volatile int* sdp_issued = reinterpret_cast<volatile int*>(drain + 7);  // [2] S^T, dP^T: tiles issued so far
+  static_assert((4 + 4 * kQS + 10 + 2 + 5 + 3) * 8 <= 512, "barrier area");
   float* vdlz = reinterpret_cast<float*>(smem + kSVec);                // [kQS][64]
   float* vzinv = reinterpret_cast<float*>(smem + kSVec + kQS * 256);   // [kQS][64]
 
@@ -215,21 +220,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&o_full[i], 1);
       mbar_init(&vec_full[i], 2);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);  // dV and dK issuers
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 2);
-      mbar_init(&sdp_full[i], 1);
+      mbar_init(&kv_empty[i], 3);
+      mbar_init(&sdp_full[i], 2);
       mbar_init(&wg_full[i], 128);
-      mbar_init(&dvk_done[i], 1);
+      mbar_init(&dvk_done[i], 2);
       mbar_init(&dq_full[i], 1);
       mbar_init(&dq_empty[i], 128);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, 2);
     mbar_init(acc_empty, 256);
-    for (int r = 0; r < 3; ++r) mbar_init(drain + r, 1);
+    for (int r = 0; r < 5; ++r) mbar_init(drain + r, 1);
     *abort_flag = 0;
+    sdp_issued[0] = sdp_issued[1] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -304,67 +310,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1 || warp >= 10) {
+  } else if (warp == 1 || warp >= 10) {  // warps 1, 10-13
     // ------------------------------------------------------------------ MMA issuers
     // One thread issues a tcgen05.mma at most every ~50 cycles (a commit costs about as much),
-    // about the execution time of an N = 64 product, so the products are spread over three warps:
-    //   warp 1   S^T, dP^T of tile g (S^T / dP^T buffer g % 2 is free once dV, dK of tile g - 2
-    //            have read W^T / G^T from it)
-    //   warp 10  dV, dK of tile g (after the pointwise group has written W^T / G^T)
-    //   warp 11  dQ of tile g (after the pointwise group has written G to shared memory)
+    // about the execution time of an N = 64 product.  The products of a tile form a chain that
+    // paces each pointwise group (W^T / G^T written -> dV, dK -> the S^T / dP^T buffer is free ->
+    // S^T, dP^T of tile g + 2 -> the group's next tile), so every product has its own warp and
+    // the two halves of each link are issued side by side:
+    //   warp 1   S^T of tile g    (S^T / dP^T buffer g % 2 is free once dV, dK of tile g - 2 have
+    //   warp 12  dP^T of tile g    read W^T / G^T from it)
+    //   warp 10  dV of tile g     (after the pointwise group has written W^T / G^T)
+    //   warp 13  dK of tile g
+    //   warp 11  dQ of tile g     (after the pointwise group has written G to shared memory)
     if (elect_one()) {
       constexpr uint32_t idSdP = idesc_f16(1, 0, 0, kBM, kBN);  // N = 64 queries, M = 128 keys
       constexpr uint32_t idAcc = idesc_f16(1, 0, 1, kD, kBN);   // A TMEM, B MN-major, N = 64
       constexpr uint32_t idDQ = idesc_f16(1, 1, 1, kD, kBM);    // A, B MN-major, M = 64, N = 64
+      // role: 0 S^T, 1 dV, 2 dQ, 3 dP^T, 4 dK
       const int role = warp == 1 ? 0 : warp - 9;
       bool ok = true;
       int k = 0, i = 0, g = 0;
       BwdItem it;
       for (; ok && bwd_next(p, k, it); ++k, ++i) {
         const int kb = i & 1;
-        if (role == 0) ok = mbar_wait(&kv_full[kb], (i >> 1) & 1, wc, 22);
+        if (role == 0 || role == 3) ok = mbar_wait(&kv_full[kb], (i >> 1) & 1, wc, 22);
         for (int t = 0; t < it.n_tiles && ok; ++t, ++g) {
           const int sb = g & 1;
           const int qs = g % kQS;
           const bool first = t == 0, last = t == it.n_tiles - 1;
-          if (role == 0) {
-            ok = mbar_wait(&q_full[qs], (g / kQS) & 1, wc, 23);
-            if (ok) ok = mbar_wait(&o_full[qs], (g / kQS) & 1, wc, 28);
+          if (role == 0 || role == 3) {
+            // S^T = K Q^T (role 0) or dP^T = V dO^T (role 3)
+            ok = mbar_wait(role == 0 ? &q_full[qs] : &o_full[qs], (g / kQS) & 1, wc, role == 0 ? 23 : 28);
             if (ok && g >= 2) ok = mbar_wait(&dvk_done[sb], ((g - 2) >> 1) & 1, wc, 24);
             if (!ok) break;
             tc_fence_after();
-            const uint64_t dK = sdesc_sw128(smem_u32(smem + kSK + kb * 32768), 16, 1024);
-            const uint64_t dV = sdesc_sw128(smem_u32(smem + kSV + kb * 32768), 16, 1024);
-            const uint64_t dQ = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 16, 1024);
-            const uint64_t ddO = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 16, 1024);
+            const uint64_t dA = sdesc_sw128(smem_u32(smem + (role == 0 ? kSK : kSV) + kb * 32768), 16, 1024);
+            const uint64_t dB = sdesc_sw128(smem_u32(smem + (role == 0 ? kSQ : kSdO) + qs * 8192), 16, 1024);
+            const uint32_t dst = tmem + (role == 0 ? kTS : kTdP) + sb * kBM;
 #pragma unroll
             for (int kk = 0; kk < kD / 16; ++kk)  // 16 head-dim elements per step: 32 B along the row
-              mma_ss(tmem + kTS + sb * kBM, dK + kk * 2, dQ + kk * 2, idSdP, kk > 0);
-#pragma unroll
-            for (int kk = 0; kk < kD / 16; ++kk)
-              mma_ss(tmem + kTdP + sb * kBM, dV + kk * 2, ddO + kk * 2, idSdP, kk > 0);
+              mma_ss(dst, dA + kk * 2, dB + kk * 2, idSdP, kk > 0);
             mma_commit(&sdp_full[sb]);
-            if (last) mma_commit(&kv_empty[kb]);  // V, and K as far as S^T is concerned
-          } else if (role == 1) {
+            sdp_issued[role == 0 ? 0 : 1] = g + 1;
+            if (last) mma_commit(&kv_empty[kb]);  // K (role 0) or V (role 3) as far as this product is concerned
+          } else if (role == 1 || role == 4) {
+            // dV += W^T dO (role 1) or dK += G^T Q (role 4)
             ok = mbar_wait(&wg_full[sb], (g >> 1) & 1, wc, 25);
             if (ok && first && i >= 1) ok = mbar_wait(acc_empty, (i - 1) & 1, wc, 27);
             if (!ok) break;
             tc_fence_after();
             // MN-major Q / dO (N = head dim); a K step of 16 queries is 16 rows = 2048 B
-            const uint64_t dQmn = sdesc_sw128(smem_u32(smem + kSQ + qs * 8192), 8192, 1024);
-            const uint64_t ddOmn = sdesc_sw128(smem_u32(smem + kSdO + qs * 8192), 8192, 1024);
+            const uint64_t dBmn = sdesc_sw128(smem_u32(smem + (role == 1 ? kSdO : kSQ) + qs * 8192), 8192, 1024);
+            const uint32_t acc = tmem + (role == 1 ? kTdV : kTdK);
+            const uint32_t a_col = tmem + (role == 1 ? kTS : kTdP) + sb * kBM;
 #pragma unroll
             for (int kk = 0; kk < kBM / 16; ++kk)  // 16 queries per step: 8 packed TMEM columns
-              mma_ts(tmem + kTdV, tmem + kTS + sb * kBM + kk * 8, ddOmn + kk * 128, idAcc, (first && kk == 0) ? 0u : 1u);
-#pragma unroll
-            for (int kk = 0; kk < kBM / 16; ++kk)
-              mma_ts(tmem + kTdK, tmem + kTdP + sb * kBM + kk * 8, dQmn + kk * 128, idAcc, (first && kk == 0) ? 0u : 1u);
+              mma_ts(acc, a_col + kk * 8, dBmn + kk * 128, idAcc, (first && kk == 0) ? 0u : 1u);
             mma_commit(&q_empty[qs]);
             mma_commit(&dvk_done[sb]);
             if (last) mma_commit(acc_full);
           } else {
             ok = mbar_wait(&wg_full[sb], (g >> 1) & 1, wc, 26);
             if (ok && g >= 2) ok = mbar_wait(&dq_empty[sb], ((g - 2) >> 1) & 1, wc, 29);
+            // dQ of tile g is read back only after the group's next tile, so it queues behind the
+            // scores of tile g + 2 (the next link of the group's chain) when tile g + 2 lies in
+            // the same item.  Never across items: the producer fetches the next item's K / V
+            // before that item's Q tiles, and that fetch waits for the buffers this item's last
+            // dQ releases, so a dQ waiting on a later item's scores would wait on itself.
+            if (ok && t + 2 < it.n_tiles) {
+              ok = wait_count(&sdp_issued[0], g + 3, wc, 33);
+              if (ok) ok = wait_count(&sdp_issued[1], g + 3, wc, 34);
+            }
             if (!ok) break;
             tc_fence_after();
             const uint64_t dG = sdesc_sw128(smem_u32(smem + kSG + (g & 3) * 16384), 16384, 1024);
@@ -510,8 +526,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const float raw = __uint_as_float(rs[e + u]);
-              wv[u] = map.prob(raw, true) * zc[e + u];
-              gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+              if constexpr (kFold) {
+                // vectors carry scale^2: W = b (b scale^2 / Z), G / 2 = b (dP^T scale^2 / Z - scale^2 delta / Z)
+                const float b = fmaxf(raw, 0.f);
+                wv[u] = (b * zc[e + u]) * b;
+                gv[u] = b * fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]);
+              } else {
+                wv[u] = map.prob(raw, true) * zc[e + u];
+                gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+              }
             }
             wpk[e / 2] = pack2<true>(wv[0], wv[1]);
             gpk[e / 2] = pack2<true>(gv[0], gv[1]);
@@ -579,10 +602,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         uint8_t* row = stg + lane * 128;
         uint32_t w[32];
+        const float f = (kFold && wg == 1) ? 2.f : 1.f;  // dK accumulated G / 2
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          w[e] = pack2<true>(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]));
-          w[16 + e] = pack2<true>(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]));
+          w[e] = pack2<true>(f * __uint_as_float(r0[2 * e]), f * __uint_as_float(r0[2 * e + 1]));
+          w[16 + e] = pack2<true>(f * __uint_as_float(r1[2 * e]), f * __uint_as_float(r1[2 * e + 1]));
         }
 #pragma unroll
         for (int c = 0; c < 8; ++c)
@@ -646,7 +670,8 @@ struct AuxParams {
   int scale_per_head, tau_per_head;
 };
 
-// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id),
+// One block per (64-row chunk, head, batch): delta_i / Z_i, 1 / Z_i (delta_i = sum_d dO_id O_id;
+// both times scale_h^2 for the plain map),
 // a zeroed dQ accumulator chunk, and the chunk's sum_i eps delta_i / Z_i (the closed-form part of
 // dscale / d gamma).  Eight lanes share a row (8 elements = 16 bytes of bf16 each), so a warp
 // reads four 128-byte rows per load instruction.
@@ -689,8 +714,11 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
     for (int off = 4; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (part == 0) {
       const float zi = i < a.T ? 1.f / a.z[bh * a.T + i] : 0.f;
-      a.dlz[row] = s * zi;
-      a.zinv[row] = zi;
+      // plain map: the main kernel expects both vectors times scale^2
+      const float sc = a.scale[a.scale_per_head ? h : 0];
+      const float f = a.purified ? 1.f : sc * sc;
+      a.dlz[row] = (s * zi) * f;
+      a.zinv[row] = zi * f;
       csum += a.eps * s * zi;
     }
   }
@@ -709,7 +737,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
   }
 }
 
-// dQ accumulator -> bf16 (one thread per 8 elements)
+// dQ accumulator -> bf16 (one thread per 8 elements); the plain map accumulated G / 2 K
 __global__ void __launch_bounds__(256) bwd_post_kernel(const AuxParams a) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int per_row = a.D / 8;
@@ -722,11 +750,12 @@ __global__ void __launch_bounds__(256) bwd_post_kernel(const AuxParams a) {
   const int h = (int)(bh % a.H), b = (int)(bh / a.H);
   const float4* src = reinterpret_cast<const float4*>(a.dq_acc + ((bh * a.Tpad + i) * a.D + c8 * 8));
   const float4 x = src[0], y = src[1];
+  const float f = a.purified ? 1.f : 2.f;
   uint4 o;
-  o.x = sm100::pack2<true>(x.x, x.y);
-  o.y = sm100::pack2<true>(x.z, x.w);
-  o.z = sm100::pack2<true>(y.x, y.y);
-  o.w = sm100::pack2<true>(y.z, y.w);
+  o.x = sm100::pack2<true>(f * x.x, f * x.y);
+  o.y = sm100::pack2<true>(f * x.z, f * x.w);
+  o.z = sm100::pack2<true>(f * y.x, f * y.y);
+  o.w = sm100::pack2<true>(f * y.z, f * y.w);
   *reinterpret_cast<uint4*>(a.dq + (int64_t)b * a.dq_s0 + (int64_t)h * a.dq_s1 + (int64_t)i * a.dq_s2 + c8 * 8) = o;
 }
 

@@ -166,3 +166,49 @@ def test_tc_backward_deterministic_mode_is_bitwise_repeatable(D):
     b = run_cuda("plain", q, k, v, do, scale, dtype=torch.bfloat16, path="tcgen05", deterministic=True)
     for name in ("dq", "dk", "dv", "dscale"):
         assert np.array_equal(a[name], b[name]), name
+
+
+@pytest.mark.parametrize("purified", [False, True])
+@pytest.mark.parametrize("shape,doc_mean", [((8, 16, 2048, 64), None), ((2, 16, 4096, 64), 300.0)],
+                         ids=["c2", "doc-masked"])
+def test_fused_and_deterministic_backward_agree_at_full_size(shape, doc_mean, purified):
+    """Benchmark-sized problems put many work items on every CTA (the cases above hold at most a
+    few), which exercises the cross-item pipelines: the fused backward must finish with a clean
+    device status and agree with the two-kernel deterministic backward."""
+    B, H, T, D = shape
+    g = torch.Generator().manual_seed(9)
+    q, k, v, do = (torch.randn(B, H, T, D, generator=g) for _ in range(4))
+    if purified:
+        q, k = (x / x.norm(dim=-1, keepdim=True) for x in (q, k))
+    q, k, v, do = (x.to("cuda", torch.bfloat16) for x in (q, k, v, do))
+    doc = None
+    if doc_mean is not None:
+        rng = np.random.default_rng(3)
+        d = np.zeros((B, T), np.int32)
+        for b in range(B):
+            t, n = 0, 0
+            while t < T:
+                L = int(rng.geometric(1 / doc_mean))
+                d[b, t:t + L] = n
+                t, n = t + L, n + 1
+        doc = torch.tensor(d, device="cuda")
+    scale = torch.linspace(6.0, 9.0, H, device="cuda") if purified else torch.full((H,), 8.0, device="cuda")
+    tau = torch.linspace(0.02, 0.08, H, device="cuda") if purified else None
+    eps = 1e-8 if purified else 1e-12
+    fwd, bwd = torch.ops.flashborn_b200.born_fwd, torch.ops.flashborn_b200.born_bwd
+    out, z = fwd(q, k, v, scale, tau, doc, True, eps, 0, 0.05, purified)
+    prev = torch.are_deterministic_algorithms_enabled()
+    res = {}
+    try:
+        for det in (False, True):
+            torch.use_deterministic_algorithms(det)
+            res[det] = bwd(do, q, k, v, out, z, scale, tau, doc, True, eps, 0, 0.05, purified)
+            torch.cuda.synchronize()
+            assert fbm.device_status() == (0, 0), f"device status after the {'split' if det else 'fused'} backward"
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    for idx, name in enumerate(("dq", "dk", "dv")):
+        a, b = res[False][idx].float(), res[True][idx].float()
+        assert torch.isfinite(a).all(), name
+        err = (a - b).abs().max().item()
+        assert err <= 1e-2 * b.abs().max().item(), (name, err, b.abs().max().item())
