@@ -13,6 +13,10 @@ on the data path); value = all ranks' FLOPs / the slowest rank's device time.
 FLOPs are algorithmic: 14 d per valid (query, key) pair (forward QK^T and PV, backward S
 recompute, dP, dV, dK, dQ), elementwise work not counted.
 
+The same run then times the end-to-end data-parallel training step of the C5 GPT (d_model 1024,
+6 layers, flash-Born attention, per-GPU batch 16 x 1024 tokens; NCCL gradient all-reduce across
+the N ranks) and reports it under ``"gpt"`` in tokens/s (``--no-gpt`` skips it).
+
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference algorithm's CPU path
 (the torch eager restatement in oracle/eager_torch.py, all host threads) on a bounded sample of
 the same workload and prints the same line with ``"impl": "reference"``.
@@ -382,6 +386,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     achieved = dom_flops / (dom_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
 
+    gpt = None if args.no_gpt else run_gpt(args, rank, world, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, units, el, threads, flops_unit = cpu_eager_sample(args.workload, args.cpu_seconds)
@@ -425,11 +431,79 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                     "steps": e2e_steps, "api": "quantumdlblocks_b200.flash_born_attention + autograd"},
             "gpu_launches": gpu_launches,
             "cpu_baseline": cpu,
+            "gpt": gpt,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_gpt(args, rank: int, world: int, dev: torch.device) -> dict:
+    """C5: data-parallel training step of the d_model 1024, 6-layer, 16 x 64-head flash-Born GPT
+    (vocab 50,257, 127 M parameters, random init from seed 0, bf16 autocast, AdamW), per-GPU batch
+    16 x 1024 tokens of Zipf(1.1) ids.  Every step copies its tokens from pinned host memory, runs
+    forward + backward + optimiser step; with N > 1 ranks DistributedDataParallel all-reduces the
+    gradients over NCCL in buckets during the backward.  Timed with CUDA events, max over ranks."""
+    from quantumdlblocks_b200.gpt import BornGPT, GPTConfig, make_ddp, param_count, train_step, zipf_tokens
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+    from quantumdlblocks_b200.sharding import max_over_ranks
+
+    cfg = GPTConfig()
+    batch = args.gpt_batch
+    torch.manual_seed(0)
+    model = BornGPT(cfg).to(dev)
+    n_params = param_count(model)
+    net = make_ddp(model, dev) if world > 1 else model
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    n_batches = 4
+    host = [torch.from_numpy(zipf_tokens(batch, cfg.seq_len, cfg.vocab_size, seed=1000 * rank + i)).pin_memory()
+            for i in range(n_batches)]
+    launches = {"n": 0}
+
+    def step(i):
+        tok = host[i % n_batches].to(dev, non_blocking=True)
+        loss = train_step(net, opt, tok)
+        return loss
+
+    for i in range(args.gpt_warmup):
+        step(i)
+    torch.cuda.synchronize()
+    losses = []
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.gpt_steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.gpt_steps):
+        ev[i][0].record()
+        losses.append(step(i))
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    (t_ms,) = max_over_ranks([t_ms], device=dev)
+    rc, site = fbm.device_status()
+    if rc != 0:
+        raise RuntimeError(f"device status {rc} (site {site}) in the GPT step")
+    tokens = world * batch * cfg.seq_len * args.gpt_steps
+    attn_flops = 14.0 * (cfg.d_model // cfg.n_heads) * cfg.seq_len * (cfg.seq_len + 1) / 2 * cfg.n_heads * cfg.n_layers
+    dense_flops = 6.0 * n_params  # per token: every weight (the tied head included) in 3 GEMMs
+    res = {
+        "metric": "gpt_train_tokens_per_s", "value": tokens / (t_ms / 1e3), "unit": "tokens/s",
+        "per_gpu": tokens / world / (t_ms / 1e3), "ms_per_step": t_ms / args.gpt_steps, "steps": args.gpt_steps,
+        "warmup": args.gpt_warmup, "n_gpus": world,
+        "config": {"workload": "C5 d_model=1024 L=6 H=16x64 seq=1024 vocab=50257 tied, flash-Born attention, "
+                               "bf16 autocast, AdamW", "per_gpu_batch": batch, "params": n_params,
+                   "data": "synthetic Zipf(1.1) token ids, host-pinned, copied every step",
+                   "allreduce": (f"NCCL via DistributedDataParallel, 25 MB buckets overlapped with the backward, "
+                                 f"{world} ranks") if world > 1 else "none (1 rank)"},
+        "model_tflops_per_gpu": (dense_flops * batch * cfg.seq_len + attn_flops * batch) * args.gpt_steps
+                                 / (t_ms / 1e3) / 1e12,
+        "loss_first_last": [float(losses[0]), float(losses[-1])],
+        "h2d_bytes_per_step": batch * (cfg.seq_len + 1) * 8,
+    }
+    del net, model, opt
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev) -> None:
@@ -495,6 +569,10 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpt", action="store_true", help="skip the C5 GPT training-step measurement")
+    ap.add_argument("--gpt-steps", type=int, default=10)
+    ap.add_argument("--gpt-warmup", type=int, default=3)
+    ap.add_argument("--gpt-batch", type=int, default=16)
     ap.add_argument("--mode", choices=["step", "fwd", "bwd"], default="step",
                     help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling)")
     args = ap.parse_args()
