@@ -7,7 +7,11 @@ unitary RoPE (``functional.py:104-121``: the two halves of each head turned by p
 angles, base 10000) and normalised again, and ``flash_born_attention`` runs with the learnable
 per-head scale clamped to [1, 100] (initialised to sqrt(hd), ``:390,429``) and eps 1e-12.  The
 rest is a plain pre-norm GPT: RMSNorm, a 4x GELU MLP, token embeddings tied to the output head.
-At d_model 1024, 6 layers, 16 heads and a 50,257-token vocabulary it has 127 M parameters.
+At d_model 1024, 6 layers, 16 heads and a 50,257-token vocabulary it has 127 M parameters.  The
+embedding table is padded to a multiple of 64 rows (50,304, the reference GPT's own default
+vocabulary size) so the output-head GEMMs have aligned leading dimensions (an odd width sends them
+to unaligned kernels several times slower); the padded logits are held at -inf, so the loss and
+every gradient equal the unpadded model's.
 
 Q, K and V stay strided views of the fused projection and O is written in ``(B, H, T, hd)`` and
 read back through a transposed view: the op takes any strides with a unit inner stride, so the
@@ -39,6 +43,7 @@ class GPTConfig:
     seq_len: int = 1024
     mlp_ratio: int = 4
     eps: float = 1e-12
+    pad_vocab_to: int = 64
 
 
 def _l2n(x: torch.Tensor, eps: float) -> torch.Tensor:
@@ -104,8 +109,13 @@ class BornGPT(nn.Module):
         if attention is None:
             from .kernels.flash_born import flash_born_attention as attention
         self.cfg = cfg
-        self.emb = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        m = max(1, cfg.pad_vocab_to)
+        rows = (cfg.vocab_size + m - 1) // m * m
+        self.emb = nn.Embedding(rows, cfg.d_model)
         nn.init.normal_(self.emb.weight, std=0.02)
+        mask = torch.zeros(rows)
+        mask[cfg.vocab_size:] = float("-inf")
+        self.register_buffer("logit_mask", mask, persistent=False)
         self.blocks = nn.ModuleList(Block(cfg, attention) for _ in range(cfg.n_layers))
         self.norm = nn.RMSNorm(cfg.d_model)
 
@@ -113,12 +123,17 @@ class BornGPT(nn.Module):
         x = self.emb(tokens)
         for blk in self.blocks:
             x = blk(x)
-        logits = F.linear(self.norm(x), self.emb.weight)  # tied output head
+        h = self.norm(x)
+        logits = F.linear(h, self.emb.weight, self.logit_mask.to(h.dtype))  # tied head, padded rows at -inf
         return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
 
 
 def param_count(model: nn.Module) -> int:
-    return sum(p.numel() for p in model.parameters())
+    """Parameters of the model as specified (the embedding rows that only pad the head excluded)."""
+    n = sum(p.numel() for p in model.parameters())
+    if isinstance(model, BornGPT):
+        n -= (model.emb.num_embeddings - model.cfg.vocab_size) * model.cfg.d_model
+    return n
 
 
 def zipf_tokens(batch: int, seq_len: int, vocab: int, s: float = 1.1, seed: int = 0) -> np.ndarray:

@@ -104,3 +104,25 @@ def test_two_gloo_ranks_train_like_one_process_on_both_batches(tmp_path):
     # fp32 sums over one batch of 6 and two averaged batches of 3 differ in their last bits; a
     # wrong reduction (a sum instead of the mean, one rank's gradient) would miss by ~lr * grad
     torch.testing.assert_close(ranks[0], _flat(model), rtol=0, atol=2e-5)
+
+
+def test_padded_head_matches_unpadded_model():
+    """Padding the tied head to a multiple of 64 rows (masked at -inf) changes no loss or gradient."""
+    import dataclasses
+
+    torch.manual_seed(1)
+    padded = BornGPT(TINY, attention=born_eager)
+    plain = BornGPT(dataclasses.replace(TINY, pad_vocab_to=1), attention=born_eager)
+    assert padded.emb.num_embeddings == 128 and plain.emb.num_embeddings == TINY.vocab_size
+    sd = padded.state_dict()
+    sd["emb.weight"] = sd["emb.weight"][:TINY.vocab_size]
+    plain.load_state_dict(sd)
+    tok = _batch(0)
+    lp = padded(tok[:, :-1], tok[:, 1:])
+    lu = plain(tok[:, :-1], tok[:, 1:])
+    lp.backward()
+    lu.backward()
+    torch.testing.assert_close(lp, lu, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(padded.emb.weight.grad[:TINY.vocab_size], plain.emb.weight.grad, rtol=1e-5, atol=1e-7)
+    assert padded.emb.weight.grad[TINY.vocab_size:].abs().max() == 0
+    assert param_count(padded) == param_count(plain)
