@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define FB_ABI_VERSION 2
+#define FB_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define FB_API __attribute__((visibility("default")))
@@ -173,6 +173,56 @@ FB_API const char* fb_last_cuda_error(void);
 
 /* FB_ABI_VERSION of the built library. */
 FB_API int fb_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * The attention layer's operand prologue (ABI version 3).  The reference builds Q, K, V with a
+ * chain of PyTorch ops (layers/attention.py:512-516 reshape / transpose / contiguous of the fused
+ * projection, :573-589 apply_unitary_rope then l2_normalize, functional.py:59-121); these kernels
+ * do it in one pass each way.
+ *
+ *   forward   Q = l2n(rope(qkv[..., 0:D])), K = l2n(rope(qkv[..., D:2D])), V = qkv[..., 2D:3D],
+ *             each written (B, H, T, hd) contiguous; D = H hd
+ *   backward  dqkv from dQ, dK, dV (B, H, T, hd) contiguous and qkv
+ *   rope      per head, element i < hd/2 and its partner i + hd/2 turn by angle (t, i):
+ *             (u_i, u_{i+hd/2}) -> (u_i cos - u_{i+hd/2} sin, u_i sin + u_{i+hd/2} cos)
+ *   l2n       y = y / sqrt(sum y^2 + eps)
+ * qkv is (B, T, 3 D) contiguous; cos / sin are (T, hd/2) contiguous fp32; hd is 64 or 128;
+ * dtype FB_BF16 or FB_F32 for qkv and every (B, H, T, hd) tensor; arithmetic in fp32.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct fb_qkv_args {
+  int32_t batch, seq_len, heads, head_dim;
+  int32_t dtype;
+  float eps;
+  const void* qkv;
+  const float* cos;
+  const float* sin;
+  void* q; /* forward: outputs; backward: the incoming gradients dQ, dK, dV */
+  void* k;
+  void* v;
+  void* dqkv; /* backward output */
+} fb_qkv_args;
+
+FB_API int fb_qkv_prologue_fwd(const fb_qkv_args* args, void* stream);
+FB_API int fb_qkv_prologue_bwd(const fb_qkv_args* args, void* stream);
+
+/* Row L2 normalisation, the layer's psi = l2_normalize(x) (functional.py:59-81):
+ *   forward   y = x / sqrt(sum x^2 + eps) over each row of `cols` elements
+ *   backward  dx = r (dy - y (y . dy)),  r = 1 / sqrt(sum x^2 + eps)
+ * Rows contiguous (row stride = cols); cols a multiple of 8 (bf16) or 4 (fp32); pointers 16-byte
+ * aligned. */
+typedef struct fb_rows_args {
+  int64_t rows;
+  int32_t cols;
+  int32_t dtype;
+  float eps;
+  const void* x;
+  void* y;
+  const void* dy;
+  void* dx;
+} fb_rows_args;
+
+FB_API int fb_l2norm_rows_fwd(const fb_rows_args* args, void* stream);
+FB_API int fb_l2norm_rows_bwd(const fb_rows_args* args, void* stream);
 
 #ifdef __cplusplus
 }

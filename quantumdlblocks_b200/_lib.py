@@ -59,8 +59,28 @@ class FbAttnArgs(ctypes.Structure):
     ]
 
 
+class FbQkvArgs(ctypes.Structure):
+    """Mirror of ``fb_qkv_args`` (the attention layer's Q / K / V prologue)."""
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("seq_len", ctypes.c_int32), ("heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("qkv", ctypes.c_void_p), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("dqkv", ctypes.c_void_p),
+    ]
+
+
+class FbRowsArgs(ctypes.Structure):
+    """Mirror of ``fb_rows_args`` (row L2 normalisation)."""
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("x", ctypes.c_void_p), ("y", ctypes.c_void_p), ("dy", ctypes.c_void_p), ("dx", ctypes.c_void_p),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 _PARGS = ctypes.POINTER(FbAttnArgs)
+_PQKV = ctypes.POINTER(FbQkvArgs)
+_PROWS = ctypes.POINTER(FbRowsArgs)
 SIGNATURES = {
     "fb_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
@@ -75,6 +95,10 @@ SIGNATURES = {
     "fb_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "fb_last_cuda_error": (ctypes.c_char_p, []),
     "fb_abi_version": (ctypes.c_int, []),
+    "fb_qkv_prologue_fwd": (ctypes.c_int, [_PQKV, ctypes.c_void_p]),
+    "fb_qkv_prologue_bwd": (ctypes.c_int, [_PQKV, ctypes.c_void_p]),
+    "fb_l2norm_rows_fwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
+    "fb_l2norm_rows_bwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
 }
 
 _lock = threading.Lock()

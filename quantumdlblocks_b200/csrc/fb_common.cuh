@@ -196,6 +196,7 @@ bool tc_bwd64_supported(const Problem& p);  // fused backward (fb_tc_bwd64.cu), 
 int tc_bwd64(const Problem& p, cudaStream_t s, int* launches);
 size_t tc_bwd64_workspace(const Problem& p);
 void record_cuda_error(cudaError_t e);
+void set_last_launch_count(int n);  // what fb_last_launch_count reports for this host thread
 // document-mask tile ranges (fb_docs.cu): bytes of workspace, and the two launches that fill it
 size_t doc_ranges_bytes(const Problem& p);
 int doc_ranges(const Problem& p, cudaStream_t s, void* ws, DocRanges* out);

@@ -13,9 +13,11 @@ vocabulary size) so the output-head GEMMs have aligned leading dimensions (an od
 to unaligned kernels several times slower); the padded logits are held at -inf, so the loss and
 every gradient equal the unpadded model's.
 
-Q, K and V stay strided views of the fused projection and O is written in ``(B, H, T, hd)`` and
-read back through a transposed view: the op takes any strides with a unit inner stride, so the
-layer makes none of the reference's ``.contiguous()`` copies (``:514-516``).
+With the native attention op the layer's operand prologue is native too: ``l2_normalize`` of the
+input and ``qkv_rope_l2norm`` (RoPE + L2 normalisation of Q and K, V copied to ``(B, H, T, hd)``)
+each run as one kernel forward and one backward, where the reference runs a chain of PyTorch ops
+(``:512-516, :573-589``).  With any other attention callable (the tests' eager restatement) the
+layer runs those ops in PyTorch on strided views.
 
 Data parallelism (``make_ddp``): one process per GPU, ``torch.nn.parallel.DistributedDataParallel``
 over NCCL, gradients all-reduced in buckets while the backward runs.
@@ -51,11 +53,12 @@ def _l2n(x: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 class BornAttention(nn.Module):
-    def __init__(self, cfg: GPTConfig, attention: Callable):
+    def __init__(self, cfg: GPTConfig, attention: Callable, fused_prologue: bool):
         super().__init__()
         d, H = cfg.d_model, cfg.n_heads
         self.H, self.hd, self.eps = H, d // H, cfg.eps
         self.attention = attention
+        self.fused_prologue = fused_prologue
         self.qkv = nn.Linear(d, 3 * d, bias=False)
         self.out = nn.Linear(d, d, bias=False)
         with torch.no_grad():
@@ -77,21 +80,26 @@ class BornAttention(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, T, D = x.shape
-        psi = _l2n(x, self.eps)
-        qkv = self.qkv(psi).view(B, T, 3, self.H, self.hd)
-        q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # (B, H, T, hd) views
-        q = _l2n(self._rope(q), self.eps)
-        k = _l2n(self._rope(k), self.eps)
+        if self.fused_prologue and x.is_cuda:
+            from .kernels.prologue import l2_normalize, qkv_rope_l2norm
+
+            q, k, v = qkv_rope_l2norm(self.qkv(l2_normalize(x, self.eps)), self.cos, self.sin, self.H, self.eps)
+        else:
+            psi = _l2n(x, self.eps)
+            qkv = self.qkv(psi).view(B, T, 3, self.H, self.hd)
+            q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # (B, H, T, hd) views
+            q = _l2n(self._rope(q), self.eps)
+            k = _l2n(self._rope(k), self.eps)
         scale = torch.clamp(self.head_scale, min=1.0, max=100.0)
         o = self.attention(q, k, v, scale=scale, is_causal=True, eps=self.eps)
         return self.out(o.transpose(1, 2).reshape(B, T, D))
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: GPTConfig, attention: Callable):
+    def __init__(self, cfg: GPTConfig, attention: Callable, fused_prologue: bool):
         super().__init__()
         d = cfg.d_model
-        self.attn = BornAttention(cfg, attention)
+        self.attn = BornAttention(cfg, attention, fused_prologue)
         self.norm = nn.RMSNorm(d)
         self.fc = nn.Linear(d, cfg.mlp_ratio * d, bias=False)
         self.proj = nn.Linear(cfg.mlp_ratio * d, d, bias=False)
@@ -102,10 +110,12 @@ class Block(nn.Module):
 
 
 class BornGPT(nn.Module):
-    """``attention`` defaults to this package's ``flash_born_attention`` (CUDA only)."""
+    """``attention`` defaults to this package's ``flash_born_attention`` (CUDA only), which also
+    switches the layers' operand prologue to the native kernels."""
 
     def __init__(self, cfg: GPTConfig, attention: Optional[Callable] = None):
         super().__init__()
+        fused = attention is None
         if attention is None:
             from .kernels.flash_born import flash_born_attention as attention
         self.cfg = cfg
@@ -116,7 +126,7 @@ class BornGPT(nn.Module):
         mask = torch.zeros(rows)
         mask[cfg.vocab_size:] = float("-inf")
         self.register_buffer("logit_mask", mask, persistent=False)
-        self.blocks = nn.ModuleList(Block(cfg, attention) for _ in range(cfg.n_layers))
+        self.blocks = nn.ModuleList(Block(cfg, attention, fused) for _ in range(cfg.n_layers))
         self.norm = nn.RMSNorm(cfg.d_model)
 
     def forward(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

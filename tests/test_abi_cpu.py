@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_strerror():
     lib = _lib.load()
-    assert lib.fb_abi_version() == 2
+    assert lib.fb_abi_version() == 3
     for code in range(0, 10):
         msg = lib.fb_strerror(code).decode()
         assert msg and (code == 0 or msg.startswith("flashborn:"))

@@ -74,3 +74,14 @@ def test_swap_rebinds_reference_names_and_restores_them(monkeypatch):
     assert sys.modules["qdlblocks.kernels.flash_born"]._run_triton_flash_born is fbm._run_triton_flash_born
     swap.uninstall()
     assert all(getattr(fake[m], n) is orig for m, ns in swap.TARGETS.items() for n in ns)
+
+
+def test_prologue_ops_raise_on_cpu_and_check_shapes():
+    from quantumdlblocks_b200.kernels.prologue import l2_normalize, qkv_rope_l2norm, rope_tables
+
+    cos, sin = rope_tables(8, 64)
+    assert cos.shape == (8, 32) and torch.allclose(cos[0], torch.ones(32)) and torch.allclose(sin[0], torch.zeros(32))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        qkv_rope_l2norm(torch.zeros(1, 8, 3 * 64), cos, sin, 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        l2_normalize(torch.zeros(2, 8))
