@@ -289,6 +289,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         return out, grads
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    if args.mode == "prologue":
+        run_prologue_mode(args, rank, flush, dev)
+        return
     if args.mode != "step":
         run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev)
         return
@@ -306,6 +309,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
+    # A device-side delay ahead of the timed steps lets the host queue them up, so that short runs
+    # (a few steps) time the device work rather than the host's first launches; it lies outside
+    # every per-step event pair.
+    torch.cuda._sleep(int(min(args.steps, 200) * 0.5e-3 * 1.9e9))
     for i in range(args.steps):
         flush.zero_()  # L2 flush (256 MiB > 126 MB L2), outside the per-step events
         ev_s[i].record()
@@ -506,6 +513,56 @@ def run_gpt(args, rank: int, world: int, dev: torch.device) -> dict:
     return res
 
 
+def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -> None:
+    """--mode prologue: the attention layer's fused operand prologue at the C5 layer shape
+    (B=16, T=1024, 16 heads x 64, bf16 projection, fp32 residual stream): qkv_prologue forward and
+    backward and the row L2 normalisation forward and backward, each timed with CUDA events after
+    an L2 flush, against the HBM roofline (algorithmic bytes: every input element read once, every
+    output element written once)."""
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+    from quantumdlblocks_b200.kernels.prologue import (_l2norm_rows, _l2norm_rows_bwd, _qkv_prologue,
+                                                       _qkv_prologue_bwd, rope_tables)
+
+    B, T, H, hd = 16, 1024, 16, 64
+    D = H * hd
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(B, T, 3 * D, generator=g, device=dev).to(torch.bfloat16)
+    cos, sin = rope_tables(T, hd, device=dev)
+    dq, dk, dv = (torch.randn(B, H, T, hd, generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+    x = torch.randn(B, T, D, generator=g, device=dev)
+    dy = torch.randn(B, T, D, generator=g, device=dev)
+    n = qkv.numel()
+    cases = {
+        "qkv_prologue_fwd": (lambda: _qkv_prologue(qkv, cos, sin, H, 1e-12), 2 * n * 2),
+        "qkv_prologue_bwd": (lambda: _qkv_prologue_bwd(qkv, cos, sin, dq, dk, dv, H, 1e-12), (n * 2 // 3 + 2 * n) * 2),
+        "l2norm_rows_fwd": (lambda: _l2norm_rows(x, 1e-12), 2 * x.numel() * 4),
+        "l2norm_rows_bwd": (lambda: _l2norm_rows_bwd(x, dy, 1e-12), 3 * x.numel() * 4),
+    }
+    peaks, src = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        for _ in range(args.warmup):
+            fn()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            fn()
+            a1.record()
+            torch.cuda.synchronize()
+            total += a0.elapsed_time(a1)
+        us = 1e3 * total / args.steps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"us": us, "bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / hbm}
+    rc, _ = fbm.device_status()
+    if rank == 0:
+        print(json.dumps({"mode": "prologue", "shape": {"B": B, "T": T, "heads": H, "head_dim": hd},
+                          "hbm_peak_gbs": hbm, "peak_source": f"hbm_gbs of {src}", "kernels": res,
+                          "device_status": rc}), flush=True)
+
+
 def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev) -> None:
     """--mode fwd|bwd: launch only the forward or only the backward kernels through the custom
     ops (one C-ABI call per step), W warm-up + K timed launches, for profilers and kernel timing."""
@@ -573,8 +630,9 @@ def main() -> None:
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-warmup", type=int, default=3)
     ap.add_argument("--gpt-batch", type=int, default=16)
-    ap.add_argument("--mode", choices=["step", "fwd", "bwd"], default="step",
-                    help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling)")
+    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue"], default="step",
+                    help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling); "
+                         "prologue: the attention layer's fused operand kernels at the C5 shape")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
