@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define FB_ABI_VERSION 3
+#define FB_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define FB_API __attribute__((visibility("default")))
@@ -82,7 +82,9 @@ typedef struct fb_attn_args {
   /* Element type of q, k, v, dout, dq, dk, dv. */
   int32_t dtype;
   /* Element type of out (the forward output; the backward reads it back for delta).
-   * Plain Born: equal to dtype. Purified Born: FB_F32 (flash_born.py:1102). */
+   * Equal to dtype, or FB_F32: purified Born writes fp32 (flash_born.py:1102); a plain forward
+   * whose output is one term of a sum of score families (complex phase, paired heads) writes
+   * fp32 so the terms combine at full precision (ABI 4). */
   int32_t out_dtype;
   int32_t is_causal;
   int32_t window_size; /* 0 = no window; else i - j < window_size */
@@ -128,6 +130,18 @@ FB_API int fb_purified_born_fwd(const fb_attn_args* args, void* stream);
 /* Purified backward: dq, dk, dv; accumulates dscale (d gamma) and dtau.
  * Replaces flash_born.py:1197-1262. */
 FB_API int fb_purified_born_bwd(const fb_attn_args* args, void* stream);
+
+/* Backward of one term of a sum of plain Born score families that share one normaliser
+ * (ABI 4).  Complex-phase Born (layers/attention.py:717-730: p = relu(a s_re)^2 + relu(a s_im)^2,
+ * s_im = <q, rot k>) and paired heads (layers/attention.py:591-626: a query row attends the keys
+ * of both heads of its pair) are such sums; each term is one plain Born problem over its own
+ * (q, k, v) views.  `out` and `z` are the WHOLE sum's forward output and Z (Z = sum over all terms
+ * and keys of p + eps); dq, dk, dv receive this term's share of the gradients (the caller adds
+ * the terms).  dscale / dtau are neither read nor written: the scale gradient of the sum is
+ * (2 / scale_h) sum_{b,i} eps delta_i / Z_i with delta_i = dO_i . O_i, formed by the caller.
+ * Same workspace as fb_born_bwd.  No single counterpart in the reference, whose complex-phase
+ * and paired-heads paths are eager PyTorch (the lines cited above). */
+FB_API int fb_born_bwd_term(const fb_attn_args* args, void* stream);
 
 /* Plain flash-Born backward that allocates nothing and takes no workspace: its scratch is a
  * fixed FB_STATIC_SCRATCH_BYTES device array inside the library (one per GPU, held from the

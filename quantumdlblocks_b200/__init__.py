@@ -8,17 +8,23 @@ signatures and tensor layout so callers swap it in unchanged (see ``swap``).
 from .kernels import (
     HAS_TRITON,
     IS_HIP,
+    complex_phase_born_attention,
     flash_born_attention,
+    flash_born_attention_token_major,
     flash_purified_born_attention,
     get_flash_born_launch_meta,
     get_rdna4_autotune_configs,
+    paired_heads_born_attention,
 )
 
 __all__ = [
     "HAS_TRITON",
     "IS_HIP",
+    "complex_phase_born_attention",
     "flash_born_attention",
+    "flash_born_attention_token_major",
     "flash_purified_born_attention",
     "get_flash_born_launch_meta",
     "get_rdna4_autotune_configs",
+    "paired_heads_born_attention",
 ]

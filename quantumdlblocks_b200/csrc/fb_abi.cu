@@ -58,17 +58,17 @@ int check_tensor(const void* p, const int64_t* st) {
 
 // Validates and normalises.  backward selects the extra backward checks; query_only (workspace
 // and path queries) fills the backward fields without requiring their pointers.
-int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, bool query_only = false) {
+int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, bool query_only = false,
+              bool given_norm = false) {
   if (a == nullptr) return FB_ERR_ARG;
   *p = Problem{};
   p->B = a->batch; p->H = a->heads; p->T = a->seq_len; p->D = a->head_dim;
   if (p->B < 0 || p->H < 0 || p->T < 0 || p->D < 1 || p->D > 256) return FB_ERR_SHAPE;
   if (p->B > 65535 || p->H > 65535) return FB_ERR_SHAPE;
   if (!valid_dtype(a->dtype) || !valid_dtype(a->out_dtype)) return FB_ERR_DTYPE;
-  // plain: out has the input type (flash_born.py:467); purified: fp32 (flash_born.py:1102) or
-  // the input type
-  if (!purified && a->out_dtype != a->dtype) return FB_ERR_DTYPE;
-  if (purified && a->out_dtype != FB_F32 && a->out_dtype != a->dtype) return FB_ERR_DTYPE;
+  // out has the input type (plain, flash_born.py:467) or fp32 (purified, flash_born.py:1102; a
+  // plain forward whose output is one partial term of a sum, combined at full precision)
+  if (a->out_dtype != FB_F32 && a->out_dtype != a->dtype) return FB_ERR_DTYPE;
   if (a->window_size < 0) return FB_ERR_ARG;
   if (a->path < FB_PATH_AUTO || a->path > FB_PATH_GENERAL) return FB_ERR_ARG;
   p->dtype = a->dtype; p->out_dtype = a->out_dtype;
@@ -109,7 +109,7 @@ int normalise(const fb_attn_args* a, bool purified, bool backward, Problem* p, b
       if ((rc = check_tensor(a->dout, a->dout_stride)) || (rc = check_tensor(a->dq, a->dq_stride)) ||
           (rc = check_tensor(a->dk, a->dk_stride)) || (rc = check_tensor(a->dv, a->dv_stride)))
         return rc;
-      if (a->dscale == nullptr) return FB_ERR_ARG;
+      if (a->dscale == nullptr && !given_norm) return FB_ERR_ARG;
       if (purified && a->dtau == nullptr) return FB_ERR_ARG;
     }
   }
@@ -134,10 +134,12 @@ size_t workspace_for(const Problem& p, int path, bool backward) {
   return use_fused_bwd(p) ? tc_bwd64_workspace(p) : tc_bwd_workspace(p);
 }
 
-int run(const fb_attn_args* a, void* stream, bool purified, bool backward) {
+int run(const fb_attn_args* a, void* stream, bool purified, bool backward, bool given_norm = false) {
   Problem p;
-  int rc = normalise(a, purified, backward, &p);
+  int rc = normalise(a, purified, backward, &p, false, given_norm);
   if (rc != FB_OK) return rc;
+  p.given_norm = given_norm;
+  if (given_norm) p.dscale = p.dtau = nullptr;
   if ((int64_t)p.B * p.H * p.T == 0) {  // nothing to do (empty batch / heads / sequence)
     t_last_launches = 0;
     return FB_OK;
@@ -179,6 +181,7 @@ int fb_born_fwd(const fb_attn_args* args, void* stream) { return fb::run(args, s
 int fb_born_bwd(const fb_attn_args* args, void* stream) { return fb::run(args, stream, false, true); }
 int fb_purified_born_fwd(const fb_attn_args* args, void* stream) { return fb::run(args, stream, true, false); }
 int fb_purified_born_bwd(const fb_attn_args* args, void* stream) { return fb::run(args, stream, true, true); }
+int fb_born_bwd_term(const fb_attn_args* args, void* stream) { return fb::run(args, stream, false, true, true); }
 
 size_t fb_bwd_workspace_size(const fb_attn_args* args) {
   fb::Problem p;

@@ -30,6 +30,9 @@ struct Problem {
   float eps, eps_base;
   bool purified;
   bool deterministic;  // backward without floating-point atomics
+  // Backward of one term of a sum of score families that share one normaliser: o and z are the
+  // whole sum's output and Z, dq/dk/dv receive this term's share, dscale/dtau are not written.
+  bool given_norm;
   Tensor4 q, k, v, o, dout, dq, dk, dv;
   float* z;
   const float* scale;

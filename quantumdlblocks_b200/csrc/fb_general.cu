@@ -37,6 +37,8 @@ struct GenArgs {
   float eps, eps_base;
   Tensor4 q, k, v, o, dout, dq, dk, dv;
   float* z;
+  int given_norm;  // backward: delta and Z from the given O and z (one term of a sum)
+  int o_f32;       // O is fp32 (else the input type)
   const float* scale;
   int scale_per_head;
   const float* tau;
@@ -383,9 +385,33 @@ __global__ void __launch_bounds__(kThreads) general_bwd_q_kernel(GenArgs a) {
     __syncthreads();
   };
 
+  if (a.given_norm) {
+    // one term of a sum of score families: delta_i = dO_i . O_i and Z_i of the whole sum
+    __syncthreads();
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int r = warp; r < BM; r += kThreads / 32) {
+      const int qi = m0 + r;
+      float acc = 0.f;
+      if (qi < a.T) {
+        for (int c = lane; c < a.D; c += 32) {
+          const int64_t off = off4(a.o, b, h, qi, c);
+          const float ov = a.o_f32 ? reinterpret_cast<const float*>(a.o.ptr)[off]
+                                   : to_f32<T>(reinterpret_cast<const T*>(a.o.ptr)[off]);
+          acc = fmaf(dOs[r * LD + c], ov, acc);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        dq_[r] = acc;
+        zq[r] = qi < a.T ? a.z[bh * a.T + qi] : 1.f;
+      }
+    }
+    __syncthreads();
+  }
   // pass 1: Z'_i = sum_j p_ij + eps and delta_i = sum_j (p_ij / Z'_i) (dO_i . v_j)
   float dsum[2] = {0.f, 0.f}, zsum[2] = {0.f, 0.f};
-  for (int n0 = lo; n0 < hi; n0 += BN) {
+  for (int n0 = a.given_norm ? hi : lo; n0 < hi; n0 += BN) {
     load_keys(n0);
     float s[2][2], dp[2][2];
     pair_products(s, dp);
@@ -409,7 +435,7 @@ __global__ void __launch_bounds__(kThreads) general_bwd_q_kernel(GenArgs a) {
     }
   }
   __syncthreads();
-  if ((tid & 15) == 0) {
+  if ((tid & 15) == 0 && !a.given_norm) {
 #pragma unroll
     for (int x = 0; x < 2; ++x) {
       const float zz = zsum[x] + a.eps;
@@ -495,6 +521,8 @@ GenArgs make_args(const Problem& p) {
   a.causal = p.causal; a.window = p.window; a.eps = p.eps; a.eps_base = p.eps_base;
   a.q = p.q; a.k = p.k; a.v = p.v; a.o = p.o; a.dout = p.dout; a.dq = p.dq; a.dk = p.dk; a.dv = p.dv;
   a.z = p.z;
+  a.given_norm = p.given_norm ? 1 : 0;
+  a.o_f32 = p.out_dtype == FB_F32 ? 1 : 0;
   a.scale = p.scale; a.scale_per_head = p.scale_per_head;
   a.tau = p.tau; a.tau_per_head = p.tau_per_head;
   a.doc = p.doc; a.doc_s0 = p.doc_s[0]; a.doc_s1 = p.doc_s[1];
@@ -545,10 +573,13 @@ int bwd_typed(const GenArgs& a, const Problem& p, cudaStream_t s, int* launches)
   if ((rc = launch(general_bwd_q_kernel<T, KD, Map>, gq, q_smem(KD), s, a)) != FB_OK) return rc;
   dim3 gkv((a.T + 31) / 32, a.H, a.B);
   if ((rc = launch(general_bwd_kv_kernel<T, KD, Map>, gkv, kv_smem(KD), s, a)) != FB_OK) return rc;
-  general_param_reduce<<<(a.H + 127) / 128, 128, 0, s>>>(a, p.dscale, p.purified ? p.dtau : nullptr);
+  *launches = 2;
+  if (!p.given_norm) {  // a term of a sum leaves the parameter gradients to its caller
+    general_param_reduce<<<(a.H + 127) / 128, 128, 0, s>>>(a, p.dscale, p.purified ? p.dtau : nullptr);
+    *launches = 3;
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
-  *launches = 3;
   return FB_OK;
 }
 

@@ -1265,9 +1265,12 @@ int tc_bwd(const Problem& pr, cudaStream_t s, int* launches) {
     rc = pr.purified ? launch_main<128, PurifiedMapTC>(pr, s, bp) : launch_main<128, PlainMapNoParam>(pr, s, bp);
   if (rc != FB_OK) return rc;
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
-  bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
-  int n = 4 + (pr.doc != nullptr ? 2 : 0);
-  if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
+  int n = 3 + (pr.doc != nullptr ? 2 : 0);
+  if (!pr.given_norm) {  // a term of a sum leaves the parameter gradients to its caller
+    bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
+    ++n;
+  }
+  if (!pr.given_norm && (!pr.scale_per_head || (pr.purified && !pr.tau_per_head))) {
     bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
     ++n;
   }

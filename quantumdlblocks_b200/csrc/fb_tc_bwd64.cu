@@ -969,9 +969,12 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   const int64_t post_threads = (int64_t)pr.B * pr.H * pr.T * (pr.D / 8);
   bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
-  bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
-  int n = 4 + (pr.doc != nullptr ? 2 : 0);
-  if (!pr.scale_per_head || (pr.purified && !pr.tau_per_head)) {
+  int n = 3 + (pr.doc != nullptr ? 2 : 0);
+  if (!pr.given_norm) {  // a term of a sum leaves the parameter gradients to its caller
+    bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
+    ++n;
+  }
+  if (!pr.given_norm && (!pr.scale_per_head || (pr.purified && !pr.tau_per_head))) {
     bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
     ++n;
   }

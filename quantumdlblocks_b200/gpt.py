@@ -91,7 +91,9 @@ class BornAttention(nn.Module):
             q = _l2n(self._rope(q), self.eps)
             k = _l2n(self._rope(k), self.eps)
         scale = torch.clamp(self.head_scale, min=1.0, max=100.0)
-        o = self.attention(q, k, v, scale=scale, is_causal=True, eps=self.eps)
+        # the native op stores O token-major, so the head merge below is a view, not a copy
+        kw = {"token_major": True} if self.fused_prologue else {}
+        o = self.attention(q, k, v, scale=scale, is_causal=True, eps=self.eps, **kw)
         return self.out(o.transpose(1, 2).reshape(B, T, D))
 
 

@@ -148,6 +148,16 @@ def _check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
         raise ValueError(f"flash-Born (B200) supports head_dim in [1, 256]; got {D}")
 
 
+def _alloc_out(B: int, H: int, T: int, D: int, dtype: torch.dtype, device: torch.device,
+               token_major: bool) -> torch.Tensor:
+    """The forward output, shape (B, H, T, D).  token_major: memory laid out (B, T, H, D), so the
+    caller's head merge ``out.transpose(1, 2).reshape(B, T, H * D)`` is a view; the kernels store
+    O rows through their strides either way."""
+    if token_major:
+        return torch.empty((B, T, H, D), dtype=dtype, device=device).transpose(1, 2)
+    return torch.empty((B, H, T, D), dtype=dtype, device=device)
+
+
 # ------------------------------------------------------------------------------------------
 # Custom ops
 # ------------------------------------------------------------------------------------------
@@ -156,10 +166,10 @@ def _check_inputs(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
 @torch.library.custom_op("flashborn_b200::born_fwd", mutates_args=())
 def _born_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: torch.Tensor, tau: Optional[torch.Tensor],
               doc_ids: Optional[torch.Tensor], is_causal: bool, eps: float, window_size: int, eps_base: float,
-              purified: bool) -> tuple[torch.Tensor, torch.Tensor]:
+              purified: bool, token_major: bool = False, f32_out: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
     B, H, T, D = q.shape
-    out_dtype = torch.float32 if purified else q.dtype
-    out = torch.empty((B, H, T, D), dtype=out_dtype, device=q.device)
+    out_dtype = torch.float32 if (purified or f32_out) else q.dtype
+    out = _alloc_out(B, H, T, D, out_dtype, q.device, token_major)
     z = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
     lib = _lib.load()
     a = _lib.FbAttnArgs()
@@ -177,9 +187,10 @@ def _born_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: torch.Te
 
 
 @_born_fwd.register_fake
-def _born_fwd_fake(q, k, v, scale, tau, doc_ids, is_causal, eps, window_size, eps_base, purified):
+def _born_fwd_fake(q, k, v, scale, tau, doc_ids, is_causal, eps, window_size, eps_base, purified, token_major=False,
+                   f32_out=False):
     B, H, T, D = q.shape
-    out = q.new_empty((B, H, T, D), dtype=torch.float32 if purified else q.dtype)
+    out = _alloc_out(B, H, T, D, torch.float32 if (purified or f32_out) else q.dtype, q.device, token_major)
     return out, q.new_empty((B, H, T), dtype=torch.float32)
 
 
@@ -219,7 +230,7 @@ def _born_bwd_fake(dout, q, k, v, out, z, scale, tau, doc_ids, is_causal, eps, w
 
 
 def _setup_context(ctx, inputs, output):
-    q, k, v, scale, tau, doc_ids, is_causal, eps, window_size, eps_base, purified = inputs
+    q, k, v, scale, tau, doc_ids, is_causal, eps, window_size, eps_base, purified = inputs[:11]
     out, z = output
     ctx.save_for_backward(q, k, v, out, z, scale, tau, doc_ids)
     ctx.is_causal = is_causal
@@ -236,7 +247,7 @@ def _backward(ctx, dout, dz):
     dq, dk, dv, dscale, dtau = _born_bwd(dout, q, k, v, out, z, scale, tau, doc_ids, ctx.is_causal, ctx.eps,
                                          ctx.window_size, ctx.eps_base, ctx.purified)
     dtau_out = dtau if (ctx.purified and tau is not None) else None
-    return dq, dk, dv, dscale, dtau_out, None, None, None, None, None, None
+    return dq, dk, dv, dscale, dtau_out, None, None, None, None, None, None, None, None
 
 
 torch.library.register_autograd("flashborn_b200::born_fwd", _backward, setup_context=_setup_context)
@@ -279,6 +290,8 @@ def flash_born_attention(
     eps: float = 1e-12,
     window_size: int = 0,
     doc_ids: torch.Tensor | None = None,
+    *,
+    token_major: bool = False,
 ) -> torch.Tensor:
     """Born attention ``O_i = sum_j p_ij v_j / (sum_j p_ij + eps)``, ``p = relu(scale q.k)^2``.
 
@@ -287,6 +300,13 @@ def flash_born_attention(
     tensor with ``H`` elements (``(H,)`` or ``(1, H, 1, 1)``), differentiable; ``window_size > 0``
     keeps keys with ``i - j < window_size``; ``doc_ids (B, T)`` masks across documents.
     Returns the output in the autocast dtype (or v's dtype) with gradients for q, k, v, scale.
+
+    ``token_major=True`` (an addition; the reference has no such argument) returns the same
+    values with memory laid out (B, T, H, D): the kernel stores each O row straight into its
+    token's slot, so the head merge that follows the reference call
+    (``out_heads.transpose(1, 2).contiguous().view(B, T, D)``, ``layers/attention.py:492``) is
+    a view instead of a copy, and the incoming gradient of that merge reaches the backward
+    kernels without a copy either.
     """
     _check_inputs(q, k, v)
     scale_t = _as_param(scale, q.device)
@@ -297,8 +317,15 @@ def flash_born_attention(
     if scale_t.numel() not in (1, q.shape[1]):
         raise ValueError(f"scale must have 1 or H={q.shape[1]} elements, got {scale_t.numel()}")
     out, _ = _born_fwd(qc, kc, vc, _flat_f32(scale_t, q.device), None, _doc_i32(doc_ids, q.device),
-                       bool(is_causal), float(eps), int(window_size), 0.0, False)
+                       bool(is_causal), float(eps), int(window_size), 0.0, False, bool(token_major))
     return out
+
+
+def flash_born_attention_token_major(q, k, v, scale, is_causal=True, eps=1e-12, window_size=0, doc_ids=None):
+    """``flash_born_attention`` with ``token_major=True``: the binding that ``swap.install`` gives
+    the reference's attention layer, whose only use of the result is the head merge of
+    ``_finalize_heads`` (``layers/attention.py:478-493``)."""
+    return flash_born_attention(q, k, v, scale, is_causal, eps, window_size, doc_ids, token_major=True)
 
 
 def _run_triton_flash_born(q, k, v, scale_t, is_causal, eps, window_size=0, doc_ids=None):

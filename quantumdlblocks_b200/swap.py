@@ -7,6 +7,9 @@ The reference binds the kernel names at import time in several modules
 module attributes to this package's implementation, so the reference's layers and GPTs
 (``SubspaceProjectorBornAttention`` and the models built on it) call the B200 kernels unchanged.
 ``uninstall()`` restores the originals.
+
+The attention layer's own binding gets the token-major variant: the layer's only use of the
+result is ``_finalize_heads``' head merge (``layers/attention.py:492``), which then costs no copy.
 """
 from __future__ import annotations
 
@@ -28,6 +31,11 @@ REPLACEMENTS = {
     "flash_born_attention": _fb.flash_born_attention,
     "flash_purified_born_attention": _fb.flash_purified_born_attention,
     "_run_triton_flash_born": _fb._run_triton_flash_born,
+}
+
+# (module, name) bindings that get a different implementation from REPLACEMENTS[name]
+LAYER_OVERRIDES = {
+    ("qdlblocks.layers.attention", "flash_born_attention"): _fb.flash_born_attention_token_major,
 }
 
 _saved: dict[tuple[str, str], object] = {}
@@ -53,7 +61,7 @@ def install(import_missing: bool = True) -> list[str]:
         for name in names:
             if hasattr(mod, name):
                 _saved.setdefault((modname, name), getattr(mod, name))
-                setattr(mod, name, REPLACEMENTS[name])
+                setattr(mod, name, LAYER_OVERRIDES.get((modname, name), REPLACEMENTS[name]))
                 patched.append(f"{modname}.{name}")
     return patched
 

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_strerror():
     lib = _lib.load()
-    assert lib.fb_abi_version() == 3
+    assert lib.fb_abi_version() == 4
     for code in range(0, 10):
         msg = lib.fb_strerror(code).decode()
         assert msg and (code == 0 or msg.startswith("flashborn:"))
@@ -82,7 +82,7 @@ def _args(**kw) -> _lib.FbAttnArgs:
         (dict(head_dim=257), _lib.FB_ERR_SHAPE),
         (dict(seq_len=-1), _lib.FB_ERR_SHAPE),
         (dict(dtype=7), _lib.FB_ERR_DTYPE),
-        (dict(out_dtype=_lib.FB_F32), _lib.FB_ERR_DTYPE),  # plain out must match the input dtype
+        (dict(out_dtype=_lib.FB_F16), _lib.FB_ERR_DTYPE),  # plain out: the input dtype or fp32
         (dict(scale=None), _lib.FB_ERR_ARG),
         (dict(scale_numel=3), _lib.FB_ERR_ARG),
         (dict(window_size=-2), _lib.FB_ERR_ARG),

@@ -70,7 +70,8 @@ def test_swap_rebinds_reference_names_and_restores_them(monkeypatch):
         monkeypatch.setitem(sys.modules, modname, m)
     patched = swap.install(import_missing=False)
     assert len(patched) == sum(len(v) for v in swap.TARGETS.values())
-    assert sys.modules["qdlblocks.layers.attention"].flash_born_attention is fbk.flash_born_attention
+    assert sys.modules["qdlblocks.layers.attention"].flash_born_attention is fbm.flash_born_attention_token_major
+    assert sys.modules["qdlblocks.kernels"].flash_born_attention is fbk.flash_born_attention
     assert sys.modules["qdlblocks.kernels.flash_born"]._run_triton_flash_born is fbm._run_triton_flash_born
     swap.uninstall()
     assert all(getattr(fake[m], n) is orig for m, ns in swap.TARGETS.items() for n in ns)
