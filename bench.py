@@ -41,6 +41,11 @@ if ROOT not in sys.path:
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+# A device-side delay (in SM clock cycles, ~0.5 ms) placed before a timed region so that the host
+# has queued the timed launches when the region starts: the events then time device work, not
+# the host's launch latency.
+HEAD_START_CYCLES = 1_000_000
+
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 WORKLOADS = {
@@ -292,6 +297,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if args.mode == "prologue":
         run_prologue_mode(args, rank, flush, dev)
         return
+    if args.mode == "families":
+        run_families_mode(args, rank, flush, dev, flops_step)
+        return
     if args.mode != "step":
         run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev)
         return
@@ -312,7 +320,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # A device-side delay ahead of the timed steps lets the host queue them up, so that short runs
     # (a few steps) time the device work rather than the host's first launches; it lies outside
     # every per-step event pair.
-    torch.cuda._sleep(int(min(args.steps, 200) * 0.5e-3 * 1.9e9))
+    torch.cuda._sleep(min(args.steps, 200) * HEAD_START_CYCLES)
     for i in range(args.steps):
         flush.zero_()  # L2 flush (256 MiB > 126 MB L2), outside the per-step events
         ev_s[i].record()
@@ -334,6 +342,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     n_fwd_launch = fbm.last_launch_count()
     for _ in range(reps):
         flush.zero_()
+        torch.cuda._sleep(HEAD_START_CYCLES)  # the host queues both launches before their events
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
         out_d, z_d = torch.ops.flashborn_b200.born_fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
@@ -352,28 +361,59 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     path_fwd = "tcgen05" if _path_is_tc(qd, False) else "general"
     path_bwd = "tcgen05" if _path_is_tc(qd, True) else "general"
 
-    # end-to-end through the public API: pinned host inputs in, outputs + grads out, every step
+    # End-to-end through the public API: every step copies its inputs from pinned host memory and
+    # its output and gradients back to pinned host memory.  The copies run on their own streams
+    # (the GPU's copy engines), pipelined across steps: step i+1's inputs stream in and step i-1's
+    # results stream out while step i computes; every byte still crosses PCIe inside the timed
+    # region, which ends when the last step's results are on the host.
     e2e_steps = max(3, min(args.steps, args.e2e_steps))
     hq, hk, hv, hdo = (x.to(bf).pin_memory() for x in (q_cpu, k_cpu, v_cpu, do_cpu))
-    h_out = [torch.empty_like(hq).pin_memory() for _ in range(4)]
+    h_out = [[torch.empty_like(hq).pin_memory() for _ in range(4)] for _ in range(2)]
+    slots = [[torch.empty(hq.shape, dtype=bf, device=dev) for _ in range(4)] for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def e2e_step():
-        xq = hq.to(dev, non_blocking=True).requires_grad_(True)
-        xk = hk.to(dev, non_blocking=True).requires_grad_(True)
-        xv = hv.to(dev, non_blocking=True).requires_grad_(True)
-        xd = hdo.to(dev, non_blocking=True)
-        out, (gq, gk, gv, _) = step(xq, xk, xv, xd)
-        for dst, src in zip(h_out, (out, gq, gk, gv)):
-            dst.copy_(src, non_blocking=True)
+    def e2e_run(n_steps: int) -> None:
+        slot_free = [None, None]    # compute finished reading a device slot's inputs
+        in_ready = [None] * n_steps
+        e0.record(comp)
+        s_in.wait_stream(comp)
+        s_out.wait_stream(comp)
 
-    e2e_step()  # untimed: first use of these buffer sizes in the caching allocator
+        def load(i):
+            with torch.cuda.stream(s_in):
+                if slot_free[i % 2] is not None:
+                    s_in.wait_event(slot_free[i % 2])
+                for dst, src in zip(slots[i % 2], (hq, hk, hv, hdo)):
+                    dst.copy_(src, non_blocking=True)
+                in_ready[i] = torch.cuda.Event()
+                in_ready[i].record(s_in)
+
+        load(0)
+        for i in range(n_steps):
+            if i + 1 < n_steps:
+                load(i + 1)
+            comp.wait_event(in_ready[i])
+            xq, xk, xv, xd = slots[i % 2]
+            out, (gq, gk, gv, _) = step(xq.detach().requires_grad_(True), xk.detach().requires_grad_(True),
+                                        xv.detach().requires_grad_(True), xd)
+            done = torch.cuda.Event()
+            done.record(comp)
+            slot_free[i % 2] = done
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for dst, src in zip(h_out[i % 2], (out, gq, gk, gv)):
+                    src.record_stream(s_out)  # the allocator keeps it until this copy ends
+                    dst.copy_(src, non_blocking=True)
+        comp.wait_stream(s_out)
+        e1.record(comp)
+
+    e2e_run(2)  # untimed: first use of these buffer sizes in the caching allocator
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
+    e2e_run(e2e_steps)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
@@ -435,7 +475,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                          "bwd_tflops": flops_bwd / (t_bwd / 1e3) / 1e12},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "api": "quantumdlblocks_b200.flash_born_attention + autograd"},
+                    "steps": e2e_steps, "api": "quantumdlblocks_b200.flash_born_attention + autograd",
+                    "copies": "pinned host buffers; H2D and D2H on two copy streams, pipelined across steps"},
             "gpu_launches": gpu_launches,
             "cpu_baseline": cpu,
             "gpt": gpt,
@@ -547,6 +588,7 @@ def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -
         total = 0.0
         for _ in range(args.steps):
             flush.zero_()
+            torch.cuda._sleep(HEAD_START_CYCLES)  # the host queues the launch before the timed region
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a0.record()
             fn()
@@ -560,6 +602,57 @@ def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -
     if rank == 0:
         print(json.dumps({"mode": "prologue", "shape": {"B": B, "T": T, "heads": H, "head_dim": hd},
                           "hbm_peak_gbs": hbm, "peak_source": f"hbm_gbs of {src}", "kernels": res,
+                          "device_status": rc}), flush=True)
+
+
+def run_families_mode(args, rank: int, flush: torch.Tensor, dev: torch.device, flops_plain: float) -> None:
+    """--mode families: complex-phase and paired-heads Born attention, forward + backward through
+    the public API at the C2 shape (B=8, H=16, N=2048, d=64, causal, bf16, unit-norm Q and K as
+    the layer passes them).  Each family is two plain terms' worth of work (complex: (q, k) and
+    (q, rot k) over all heads; paired: four head-half terms over H/2 heads), so its algorithmic
+    FLOPs are 2 x the plain C2 step's; timed with CUDA events after an L2 flush."""
+    from quantumdlblocks_b200 import complex_phase_born_attention, paired_heads_born_attention
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+
+    B, H, N, D = 8, 16, 2048, 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    q, k = (torch.nn.functional.normalize(torch.randn(B, H, N, D, generator=g, device=dev), dim=-1) for _ in range(2))
+    v = torch.randn(B, H, N, D, generator=g, device=dev)
+    q, k, v = (x.to(torch.bfloat16).requires_grad_(True) for x in (q, k, v))
+    do = torch.randn(B, H, N, D, generator=g, device=dev).to(torch.bfloat16)
+    cases = {
+        "complex_phase": (complex_phase_born_attention, torch.full((1, H, 1, 1), 8.0, device=dev)),
+        "paired_heads": (paired_heads_born_attention, torch.full((1, H // 2, 1, 1), 8.0, device=dev)),
+    }
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    res = {}
+    for name, (fn, sc) in cases.items():
+        sc = sc.requires_grad_(True)
+
+        def step():
+            out = fn(q, k, v, sc, is_causal=True, eps=1e-12)
+            return torch.autograd.grad(out, (q, k, v, sc), do)
+
+        for _ in range(args.warmup):
+            step()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda._sleep(4 * HEAD_START_CYCLES)  # the host queues the step before the timed region
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record()
+            step()
+            a1.record()
+            torch.cuda.synchronize()
+            total += a0.elapsed_time(a1)
+        ms = total / args.steps
+        tf = 2.0 * flops_plain / (ms / 1e3) / 1e12
+        res[name] = {"ms": ms, "flops": 2.0 * flops_plain, "tflops": tf, "frac_bf16_peak": tf / peak}
+    rc, _ = fbm.device_status()
+    if rank == 0:
+        print(json.dumps({"mode": "families", "shape": {"B": B, "H": H, "N": N, "D": D, "causal": True},
+                          "peak_tflops": peak, "peak_source": f"bf16_tflops (burst) of {src}", "families": res,
                           "device_status": rc}), flush=True)
 
 
@@ -586,6 +679,7 @@ def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs,
     total = 0.0
     for _ in range(args.steps):
         flush.zero_()
+        torch.cuda._sleep(HEAD_START_CYCLES)  # the host queues the launch before the timed region
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         one()
@@ -630,9 +724,10 @@ def main() -> None:
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-warmup", type=int, default=3)
     ap.add_argument("--gpt-batch", type=int, default=16)
-    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue"], default="step",
+    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue", "families"], default="step",
                     help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling); "
-                         "prologue: the attention layer's fused operand kernels at the C5 shape")
+                         "prologue: the attention layer's fused operand kernels at the C5 shape; "
+                         "families: complex-phase and paired-heads attention at the C2 shape")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

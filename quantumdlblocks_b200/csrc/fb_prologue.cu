@@ -12,10 +12,11 @@
 //   l2norm_rows_fwd    y = x / sqrt(sum x^2 + eps) per row
 //   l2norm_rows_bwd    dx = r (dy - y (y . dy)), r = 1 / sqrt(sum x^2 + eps)
 //
-// One warp per token row.  In the prologue lane l holds elements [l E, l E + E) of a head (E =
-// hd / 32); the RoPE partner of element i < hd / 2 is element i + hd / 2, which sits 16 lanes away,
-// so one shfl.xor 16 brings it.  Sums of squares and the backward's dot products are warp
-// reductions; all arithmetic is fp32, inputs and outputs bf16 or fp32.  Memory-bound: each
+// One warp per token row, 16-byte accesses.  In the prologue a head spans hd / 8 (bf16) or hd / 4
+// (fp32) lanes and one warp-wide access covers several heads; the RoPE partner of element
+// i < hd / 2 is element i + hd / 2, half a head's lanes away, so one shfl.xor brings it.  Sums of
+// squares and the backward's dot products are reductions over a head's lanes; all arithmetic is
+// fp32, inputs and outputs bf16 or fp32.  Memory-bound: each
 // kernel reads and writes every element once (the row L2 kernels read x twice, the second time
 // from L1).
 #include <cuda_runtime.h>
@@ -27,180 +28,18 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
-template <typename T, int E> struct Lane;
-template <> struct Lane<__nv_bfloat16, 2> {
-  __device__ static void load(const __nv_bfloat16* p, float (&f)[2]) {
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
-    f[0] = __uint_as_float(w << 16);
-    f[1] = __uint_as_float(w & 0xFFFF0000u);
-  }
-  __device__ static void store(__nv_bfloat16* p, const float (&f)[2]) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(f[0], f[1]);
-    *reinterpret_cast<__nv_bfloat162*>(p) = v;
-  }
-};
-template <> struct Lane<__nv_bfloat16, 4> {
-  __device__ static void load(const __nv_bfloat16* p, float (&f)[4]) {
-    const uint2 w = *reinterpret_cast<const uint2*>(p);
-    f[0] = __uint_as_float(w.x << 16);
-    f[1] = __uint_as_float(w.x & 0xFFFF0000u);
-    f[2] = __uint_as_float(w.y << 16);
-    f[3] = __uint_as_float(w.y & 0xFFFF0000u);
-  }
-  __device__ static void store(__nv_bfloat16* p, const float (&f)[4]) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), b = __floats2bfloat162_rn(f[2], f[3]);
-    uint2 w;
-    w.x = *reinterpret_cast<uint32_t*>(&a);
-    w.y = *reinterpret_cast<uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(p) = w;
-  }
-};
-template <> struct Lane<float, 2> {
-  __device__ static void load(const float* p, float (&f)[2]) {
-    const float2 v = *reinterpret_cast<const float2*>(p);
-    f[0] = v.x;
-    f[1] = v.y;
-  }
-  __device__ static void store(float* p, const float (&f)[2]) { *reinterpret_cast<float2*>(p) = make_float2(f[0], f[1]); }
-};
-template <> struct Lane<float, 4> {
-  __device__ static void load(const float* p, float (&f)[4]) {
-    const float4 v = *reinterpret_cast<const float4*>(p);
-    f[0] = v.x;
-    f[1] = v.y;
-    f[2] = v.z;
-    f[3] = v.w;
-  }
-  __device__ static void store(float* p, const float (&f)[4]) {
-    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
-  }
-};
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
-struct QkvParams {
-  int B, T, H;
-  float eps;
-  const void* qkv;   // (B, T, 3 H hd) contiguous
-  const float* cos;  // (T, hd / 2) contiguous
-  const float* sin;
-  void* q;           // (B, H, T, hd) contiguous: forward outputs / backward incoming gradients
-  void* k;
-  void* v;
-  void* dqkv;        // backward output, qkv's layout
-};
-
-// Rotation of this lane's E elements: for the first half of the head (lanes 0-15)
-// y = u c - u' s, for the second half y = u' s + u c, u' = the partner element 16 lanes away.
-template <int E>
-__device__ __forceinline__ void rope(const float (&u)[E], const float (&c)[E], const float (&s)[E], bool hi,
-                                     float (&y)[E]) {
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float o = __shfl_xor_sync(0xffffffffu, u[e], 16);
-    y[e] = hi ? fmaf(o, s[e], u[e] * c[e]) : fmaf(u[e], c[e], -o * s[e]);
-  }
-}
-
-template <typename T, int HD>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) qkv_prologue_fwd_kernel(const QkvParams p) {
-  constexpr int E = HD / 32;
-  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
-  if (row >= (int64_t)p.B * p.T) return;
-  const int lane = threadIdx.x & 31;
-  const int b = (int)(row / p.T), t = (int)(row % p.T);
-  const int D = p.H * HD;
-  const T* src = static_cast<const T*>(p.qkv) + row * 3 * D + lane * E;
-  float c[E], s[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const int pi = (lane & 15) * E + e;  // rotation pair of this element
-    c[e] = p.cos[(int64_t)t * (HD / 2) + pi];
-    s[e] = p.sin[(int64_t)t * (HD / 2) + pi];
-  }
-  const bool hi = lane >= 16;
-  for (int part = 0; part < 3; ++part) {
-    T* dst = static_cast<T*>(part == 0 ? p.q : part == 1 ? p.k : p.v) + ((int64_t)b * p.H * p.T + t) * HD + lane * E;
-#pragma unroll 4
-    for (int h = 0; h < p.H; ++h) {
-      float u[E];
-      Lane<T, E>::load(src + part * D + h * HD, u);
-      if (part < 2) {
-        float y[E];
-        rope<E>(u, c, s, hi, y);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) ss = fmaf(y[e], y[e], ss);
-        const float r = rsqrtf(warp_sum(ss) + p.eps);
-#pragma unroll
-        for (int e = 0; e < E; ++e) u[e] = y[e] * r;
-      }
-      Lane<T, E>::store(dst + (int64_t)h * p.T * HD, u);
-    }
-  }
-}
-
-template <typename T, int HD>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32) qkv_prologue_bwd_kernel(const QkvParams p) {
-  constexpr int E = HD / 32;
-  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
-  if (row >= (int64_t)p.B * p.T) return;
-  const int lane = threadIdx.x & 31;
-  const int b = (int)(row / p.T), t = (int)(row % p.T);
-  const int D = p.H * HD;
-  const T* src = static_cast<const T*>(p.qkv) + row * 3 * D + lane * E;
-  T* out = static_cast<T*>(p.dqkv) + row * 3 * D + lane * E;
-  float c[E], s[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const int pi = (lane & 15) * E + e;
-    c[e] = p.cos[(int64_t)t * (HD / 2) + pi];
-    s[e] = p.sin[(int64_t)t * (HD / 2) + pi];
-  }
-  const bool hi = lane >= 16;
-  for (int part = 0; part < 3; ++part) {
-    const T* g = static_cast<const T*>(part == 0 ? p.q : part == 1 ? p.k : p.v) + ((int64_t)b * p.H * p.T + t) * HD +
-                 lane * E;
-#pragma unroll 4
-    for (int h = 0; h < p.H; ++h) {
-      float dz[E];
-      Lane<T, E>::load(g + (int64_t)h * p.T * HD, dz);
-      if (part < 2) {
-        float u[E], y[E];
-        Lane<T, E>::load(src + part * D + h * HD, u);
-        rope<E>(u, c, s, hi, y);
-        float ss = 0.f, yd = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          ss = fmaf(y[e], y[e], ss);
-          yd = fmaf(y[e], dz[e], yd);
-        }
-        const float r = rsqrtf(warp_sum(ss) + p.eps);
-        const float k3 = r * r * r * warp_sum(yd);
-        // d y = r dz - y r^3 (y . dz); then the transposed rotation: du = dy c + dy' s (first
-        // half) and du = dy c - dy' s (second half), dy' = the partner's gradient
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float dy = fmaf(r, dz[e], -y[e] * k3);
-          const float o = __shfl_xor_sync(0xffffffffu, dy, 16);
-          dz[e] = hi ? fmaf(dy, c[e], -o * s[e]) : fmaf(dy, c[e], o * s[e]);
-        }
-      }
-      Lane<T, E>::store(out + part * D + h * HD, dz);
-    }
-  }
-}
-
 // Row L2 normalisation: one warp per row, 16-byte chunks (8 bf16 / 4 fp32 elements).
 template <typename T> struct Chunk;
 template <> struct Chunk<__nv_bfloat16> {
   static constexpr int N = 8;
-  __device__ static void load(const __nv_bfloat16* p, float (&f)[8]) {
-    const uint4 w = *reinterpret_cast<const uint4*>(p);
+  __device__ static void load(const __nv_bfloat16* p, float (&f)[8]) { unpack(*reinterpret_cast<const uint4*>(p), f); }
+  __device__ static void unpack(const uint4 w, float (&f)[8]) {
     const uint32_t a[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -220,17 +59,167 @@ template <> struct Chunk<__nv_bfloat16> {
 };
 template <> struct Chunk<float> {
   static constexpr int N = 4;
-  __device__ static void load(const float* p, float (&f)[4]) {
-    const float4 v = *reinterpret_cast<const float4*>(p);
-    f[0] = v.x;
-    f[1] = v.y;
-    f[2] = v.z;
-    f[3] = v.w;
+  __device__ static void load(const float* p, float (&f)[4]) { unpack(*reinterpret_cast<const uint4*>(p), f); }
+  __device__ static void unpack(const uint4 w, float (&f)[4]) {
+    f[0] = __uint_as_float(w.x);
+    f[1] = __uint_as_float(w.y);
+    f[2] = __uint_as_float(w.z);
+    f[3] = __uint_as_float(w.w);
   }
   __device__ static void store(float* p, const float (&f)[4]) {
     *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
   }
 };
+
+struct QkvParams {
+  int B, T, H;
+  float eps;
+  const void* qkv;   // (B, T, 3 H hd) contiguous
+  const float* cos;  // (T, hd / 2) contiguous
+  const float* sin;
+  void* q;           // (B, H, T, hd) contiguous: forward outputs / backward incoming gradients
+  void* k;
+  void* v;
+  void* dqkv;        // backward output, qkv's layout
+};
+
+// The prologue works in 16-byte chunks: N elements per lane (8 bf16 or 4 fp32), LPH = hd / N
+// lanes per head, 32 / LPH heads per warp-wide access.  Element i < hd / 2 of a head and its RoPE
+// partner i + hd / 2 sit LPH / 2 lanes apart (one shfl.xor); a head's norm is a reduction over its
+// LPH lanes.  Each lane loads G chunks before it computes, so a warp keeps G x 512 bytes of loads
+// in flight.
+template <typename T, int HD> struct QkvShape {
+  static constexpr int N = Chunk<T>::N;
+  static constexpr int LPH = HD / N;     // lanes per head
+  static constexpr int HPP = 32 / LPH;   // heads per warp-wide access
+  static constexpr int G = 4;            // accesses in flight per lane
+  static_assert(LPH >= 2 && LPH <= 32, "head must span 2..32 lanes");
+};
+
+template <int LPH>
+__device__ __forceinline__ float head_sum(float v) {
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) qkv_prologue_fwd_kernel(const QkvParams p) {
+  using S = QkvShape<T, HD>;
+  constexpr int N = S::N, LPH = S::LPH, HPP = S::HPP, G = S::G;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= (int64_t)p.B * p.T) return;  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPH, hl = lane / LPH;
+  const bool hi = sub >= LPH / 2;
+  const int b = (int)(row / p.T), t = (int)(row % p.T);
+  const int D = p.H * HD;
+  const T* __restrict__ src = static_cast<const T*>(p.qkv) + row * 3 * D + sub * N;
+  float c[N], sn[N];
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    const int pi = (sub % (LPH / 2)) * N + e;  // rotation pair of this element
+    c[e] = p.cos[(int64_t)t * (HD / 2) + pi];
+    sn[e] = p.sin[(int64_t)t * (HD / 2) + pi];
+  }
+  for (int part = 0; part < 3; ++part) {
+    T* __restrict__ dst = static_cast<T*>(part == 0 ? p.q : part == 1 ? p.k : p.v) +
+                          ((int64_t)b * p.H * p.T + t) * HD + sub * N;
+    for (int h0 = 0; h0 < p.H; h0 += G * HPP) {
+      uint4 raw[G];  // loaded chunks stay packed until used (fewer registers, more rows in flight)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int h = h0 + g * HPP + hl;
+        raw[g] = h < p.H ? *reinterpret_cast<const uint4*>(src + part * D + h * HD) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int h = h0 + g * HPP + hl;
+        if (part == 2) {  // V: copied
+          if (h < p.H) *reinterpret_cast<uint4*>(dst + (int64_t)h * p.T * HD) = raw[g];
+          continue;
+        }
+        float u[N], y[N], ss = 0.f;
+        Chunk<T>::unpack(raw[g], u);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float o = __shfl_xor_sync(0xffffffffu, u[e], LPH / 2);
+          y[e] = hi ? fmaf(o, sn[e], u[e] * c[e]) : fmaf(u[e], c[e], -o * sn[e]);
+          ss = fmaf(y[e], y[e], ss);
+        }
+        const float r = rsqrtf(head_sum<LPH>(ss) + p.eps);
+#pragma unroll
+        for (int e = 0; e < N; ++e) y[e] *= r;
+        if (h < p.H) Chunk<T>::store(dst + (int64_t)h * p.T * HD, y);
+      }
+    }
+  }
+}
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) qkv_prologue_bwd_kernel(const QkvParams p) {
+  using S = QkvShape<T, HD>;
+  constexpr int N = S::N, LPH = S::LPH, HPP = S::HPP, G = S::G;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= (int64_t)p.B * p.T) return;  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPH, hl = lane / LPH;
+  const bool hi = sub >= LPH / 2;
+  const int b = (int)(row / p.T), t = (int)(row % p.T);
+  const int D = p.H * HD;
+  const T* __restrict__ src = static_cast<const T*>(p.qkv) + row * 3 * D + sub * N;
+  T* __restrict__ out = static_cast<T*>(p.dqkv) + row * 3 * D + sub * N;
+  float c[N], sn[N];
+#pragma unroll
+  for (int e = 0; e < N; ++e) {
+    const int pi = (sub % (LPH / 2)) * N + e;
+    c[e] = p.cos[(int64_t)t * (HD / 2) + pi];
+    sn[e] = p.sin[(int64_t)t * (HD / 2) + pi];
+  }
+  for (int part = 0; part < 3; ++part) {
+    const T* __restrict__ grad = static_cast<const T*>(part == 0 ? p.q : part == 1 ? p.k : p.v) +
+                                 ((int64_t)b * p.H * p.T + t) * HD + sub * N;
+    for (int h0 = 0; h0 < p.H; h0 += G * HPP) {
+      uint4 rd[G], ru[G];  // loaded chunks stay packed until used
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int h = h0 + g * HPP + hl;
+        const bool ok = h < p.H;
+        rd[g] = ok ? *reinterpret_cast<const uint4*>(grad + (int64_t)h * p.T * HD) : make_uint4(0, 0, 0, 0);
+        ru[g] = ok && part < 2 ? *reinterpret_cast<const uint4*>(src + part * D + h * HD) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const int h = h0 + g * HPP + hl;
+        if (part == 2) {  // V was copied: its gradient passes through
+          if (h < p.H) *reinterpret_cast<uint4*>(out + part * D + h * HD) = rd[g];
+          continue;
+        }
+        float dz[N], u[N], y[N], ss = 0.f, yd = 0.f;
+        Chunk<T>::unpack(rd[g], dz);
+        Chunk<T>::unpack(ru[g], u);
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float o = __shfl_xor_sync(0xffffffffu, u[e], LPH / 2);
+          y[e] = hi ? fmaf(o, sn[e], u[e] * c[e]) : fmaf(u[e], c[e], -o * sn[e]);
+          ss = fmaf(y[e], y[e], ss);
+          yd = fmaf(y[e], dz[e], yd);
+        }
+        const float r = rsqrtf(head_sum<LPH>(ss) + p.eps);
+        const float k3 = r * r * r * head_sum<LPH>(yd);
+        // d y = r dz - y r^3 (y . dz); then the transposed rotation: du = dy c + dy' s (first
+        // half) and du = dy c - dy' s (second half), dy' = the partner's gradient
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float dy = fmaf(r, dz[e], -y[e] * k3);
+          const float o = __shfl_xor_sync(0xffffffffu, dy, LPH / 2);
+          dz[e] = hi ? fmaf(dy, c[e], -o * sn[e]) : fmaf(dy, c[e], o * sn[e]);
+        }
+        if (h < p.H) Chunk<T>::store(out + part * D + h * HD, dz);
+      }
+    }
+  }
+}
 
 struct RowsParams {
   int64_t rows;
