@@ -300,6 +300,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if args.mode == "families":
         run_families_mode(args, rank, flush, dev, flops_step)
         return
+    if args.mode == "gpt":
+        gpt = run_gpt(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(gpt), flush=True)
+        return
     if args.mode != "step":
         run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev)
         return
@@ -639,7 +644,7 @@ def run_families_mode(args, rank: int, flush: torch.Tensor, dev: torch.device, f
         total = 0.0
         for _ in range(args.steps):
             flush.zero_()
-            torch.cuda._sleep(4 * HEAD_START_CYCLES)  # the host queues the step before the timed region
+            torch.cuda._sleep(16 * HEAD_START_CYCLES)  # the host queues the step before the timed region
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a0.record()
             step()
@@ -724,10 +729,11 @@ def main() -> None:
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-warmup", type=int, default=3)
     ap.add_argument("--gpt-batch", type=int, default=16)
-    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue", "families"], default="step",
+    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue", "families", "gpt"], default="step",
                     help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling); "
                          "prologue: the attention layer's fused operand kernels at the C5 shape; "
-                         "families: complex-phase and paired-heads attention at the C2 shape")
+                         "families: complex-phase and paired-heads attention at the C2 shape; "
+                         "gpt: only the C5 GPT training step")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -143,6 +143,53 @@ FB_API int fb_purified_born_bwd(const fb_attn_args* args, void* stream);
  * and paired-heads paths are eager PyTorch (the lines cited above). */
 FB_API int fb_born_bwd_term(const fb_attn_args* args, void* stream);
 
+/* Glue of the families run as sums of plain Born terms (ABI 4); no counterpart in the reference,
+ * whose complex-phase and paired-heads paths are eager PyTorch (layers/attention.py:717-730,
+ * :591-626).
+ *   fb_rotate_halves   dst = a + R b per row of head_dim = 2 h elements, R b = [-b_im | b_re]
+ *                      (adjoint = 0: the key of the imaginary overlap <q, R k> = q_im.k_re - q_re.k_im)
+ *                      or R^T b = [b_im | -b_re] (adjoint = 1: its gradient); a may be NULL; rows
+ *                      contiguous, a / b / dst of one dtype
+ *   fb_combine_terms   O = sum_t O_t Z_t / sum_t Z_t, Z = sum_t Z_t over n_terms (1..4) term outputs
+ *                      O_t (B, H, T, D) fp32 contiguous (16-byte aligned) and Z_t (B, H, T) fp32
+ *                      contiguous; O written as out_dtype through out_stride, Z through z_stride
+ *   fb_delta_terms     part[b, h] = sum_t eps (dO . O) / Z over (b, h)'s rows: the family's scale
+ *                      gradient is (2 / scale) times the sum of part over the rows that scale
+ *                      entry serves (Z contiguous (B, H, T); part (B, H) fp32) */
+typedef struct fb_rot_args {
+  int64_t rows;
+  int32_t head_dim;
+  int32_t dtype;
+  int32_t adjoint;
+  const void* a;
+  const void* b;
+  void* dst;
+} fb_rot_args;
+
+typedef struct fb_combine_args {
+  int32_t batch, heads, seq_len, head_dim;
+  int32_t n_terms;
+  int32_t out_dtype;
+  const float* o[4];
+  const float* z[4];
+  void* out;    int64_t out_stride[4];
+  float* z_out; int64_t z_stride[3];
+} fb_combine_args;
+
+typedef struct fb_delta_args {
+  int32_t batch, heads, seq_len, head_dim;
+  int32_t dout_dtype, out_dtype;
+  float eps;
+  const void* dout; int64_t dout_stride[4];
+  const void* out;  int64_t out_stride[4];
+  const float* z;
+  float* part;
+} fb_delta_args;
+
+FB_API int fb_rotate_halves(const fb_rot_args* args, void* stream);
+FB_API int fb_combine_terms(const fb_combine_args* args, void* stream);
+FB_API int fb_delta_terms(const fb_delta_args* args, void* stream);
+
 /* Plain flash-Born backward that allocates nothing and takes no workspace: its scratch is a
  * fixed FB_STATIC_SCRATCH_BYTES device array inside the library (one per GPU, held from the
  * first call on that GPU until exit).  For callers that cannot allocate device memory (a host
@@ -237,6 +284,33 @@ typedef struct fb_rows_args {
 
 FB_API int fb_l2norm_rows_fwd(const fb_rows_args* args, void* stream);
 FB_API int fb_l2norm_rows_bwd(const fb_rows_args* args, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * The GPT training loss (ABI version 4): mean cross-entropy over bf16 logits, replacing
+ * F.cross_entropy(logits.reshape(-1, V), targets) of the reference's GPTs
+ * (models/born_gpt.py:1291), which under bf16 autocast runs over an fp32 copy of the logits.
+ *   forward   lse[r] = log sum_c exp(x[r, c]),  loss[r] = lse[r] - x[r, targets[r]]
+ *             (the caller averages loss over the rows)
+ *   backward  grad[r, c] = (exp(x[r, c] - lse[r]) - [c == targets[r]]) * gscale[0] / rows
+ * logits and grad are bf16 rows of `vocab` elements `ld` apart (vocab and ld multiples of 8,
+ * pointers 16-byte aligned); columns holding -inf take no probability.  targets are int64; a
+ * target outside [0, vocab) gives a NaN loss.  lse and loss are fp32 (rows); gscale is a device
+ * fp32 scalar (the incoming gradient of the mean loss).
+ * ------------------------------------------------------------------------------------------ */
+typedef struct fb_xent_args {
+  int64_t rows;
+  int32_t vocab;
+  int64_t ld;
+  const void* logits;
+  const int64_t* targets;
+  float* lse;
+  float* loss;         /* forward output */
+  void* grad;          /* backward output */
+  const float* gscale; /* backward input */
+} fb_xent_args;
+
+FB_API int fb_xent_fwd(const fb_xent_args* args, void* stream);
+FB_API int fb_xent_bwd(const fb_xent_args* args, void* stream);
 
 #ifdef __cplusplus
 }

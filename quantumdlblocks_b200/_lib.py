@@ -77,10 +77,46 @@ class FbRowsArgs(ctypes.Structure):
     ]
 
 
+class FbXentArgs(ctypes.Structure):
+    """Mirror of ``fb_xent_args`` (the GPT training loss)."""
+    _fields_ = [
+        ("rows", ctypes.c_int64), ("vocab", ctypes.c_int32), ("ld", ctypes.c_int64),
+        ("logits", ctypes.c_void_p), ("targets", ctypes.c_void_p), ("lse", ctypes.c_void_p),
+        ("loss", ctypes.c_void_p), ("grad", ctypes.c_void_p), ("gscale", ctypes.c_void_p),
+    ]
+
+
+class FbRotArgs(ctypes.Structure):
+    """Mirror of ``fb_rot_args``."""
+    _fields_ = [("rows", ctypes.c_int64), ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32),
+                ("adjoint", ctypes.c_int32), ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("dst", ctypes.c_void_p)]
+
+
+class FbCombineArgs(ctypes.Structure):
+    """Mirror of ``fb_combine_args``."""
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("n_terms", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("o", ctypes.c_void_p * 4), ("z", ctypes.c_void_p * 4),
+        ("out", ctypes.c_void_p), ("out_stride", _I64x4), ("z_out", ctypes.c_void_p), ("z_stride", ctypes.c_int64 * 3),
+    ]
+
+
+class FbDeltaArgs(ctypes.Structure):
+    """Mirror of ``fb_delta_args``."""
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("dout_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float), ("dout", ctypes.c_void_p), ("dout_stride", _I64x4),
+        ("out", ctypes.c_void_p), ("out_stride", _I64x4), ("z", ctypes.c_void_p), ("part", ctypes.c_void_p),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 _PARGS = ctypes.POINTER(FbAttnArgs)
 _PQKV = ctypes.POINTER(FbQkvArgs)
 _PROWS = ctypes.POINTER(FbRowsArgs)
+_PXENT = ctypes.POINTER(FbXentArgs)
 SIGNATURES = {
     "fb_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
@@ -100,6 +136,11 @@ SIGNATURES = {
     "fb_qkv_prologue_bwd": (ctypes.c_int, [_PQKV, ctypes.c_void_p]),
     "fb_l2norm_rows_fwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
     "fb_l2norm_rows_bwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
+    "fb_xent_fwd": (ctypes.c_int, [_PXENT, ctypes.c_void_p]),
+    "fb_rotate_halves": (ctypes.c_int, [ctypes.POINTER(FbRotArgs), ctypes.c_void_p]),
+    "fb_combine_terms": (ctypes.c_int, [ctypes.POINTER(FbCombineArgs), ctypes.c_void_p]),
+    "fb_delta_terms": (ctypes.c_int, [ctypes.POINTER(FbDeltaArgs), ctypes.c_void_p]),
+    "fb_xent_bwd": (ctypes.c_int, [_PXENT, ctypes.c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -17,7 +17,10 @@ With the native attention op the layer's operand prologue is native too: ``l2_no
 input and ``qkv_rope_l2norm`` (RoPE + L2 normalisation of Q and K, V copied to ``(B, H, T, hd)``)
 each run as one kernel forward and one backward, where the reference runs a chain of PyTorch ops
 (``:512-516, :573-589``).  With any other attention callable (the tests' eager restatement) the
-layer runs those ops in PyTorch on strided views.
+layer runs those ops in PyTorch on strided views.  The native attention op stores O token-major,
+so the head merge before the output projection is a view, and the loss is the native fused
+cross-entropy over the bf16 logits (the reference's ``F.cross_entropy``, ``models/born_gpt.py:1291``,
+runs over an fp32 copy of them).
 
 Data parallelism (``make_ddp``): one process per GPU, ``torch.nn.parallel.DistributedDataParallel``
 over NCCL, gradients all-reduced in buckets while the backward runs.
@@ -118,6 +121,7 @@ class BornGPT(nn.Module):
     def __init__(self, cfg: GPTConfig, attention: Optional[Callable] = None):
         super().__init__()
         fused = attention is None
+        self.native_loss = fused  # with the native attention, the loss runs on the native kernels too
         if attention is None:
             from .kernels.flash_born import flash_born_attention as attention
         self.cfg = cfg
@@ -137,7 +141,12 @@ class BornGPT(nn.Module):
             x = blk(x)
         h = self.norm(x)
         logits = F.linear(h, self.emb.weight, self.logit_mask.to(h.dtype))  # tied head, padded rows at -inf
-        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+        logits = logits.view(-1, logits.shape[-1])
+        if self.native_loss and logits.is_cuda and logits.dtype == torch.bfloat16:
+            from .kernels.xent import cross_entropy
+
+            return cross_entropy(logits, targets.reshape(-1))
+        return F.cross_entropy(logits.float(), targets.reshape(-1))
 
 
 def param_count(model: nn.Module) -> int:

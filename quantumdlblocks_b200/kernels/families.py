@@ -16,10 +16,12 @@ at every visible token.  The four terms are plain Born problems over the head ha
 (q_a, k_b, v_b), a, b in {0, 1}, with the token-level causal / window / document mask.
 
 Combine.  Each term runs with eps / (number of terms) and fp32 output, so that for every query
-row ``Z = sum_t Z_t`` is the family's ``sum p + eps`` and ``O = sum_t O_t Z_t / Z``.  The
-backward runs ``fb_born_bwd_term`` per term with the combined O and Z (the term's share of
-dQ, dK, dV) and forms the scale gradient from the closed form of a score homogeneous of
-degree 2 in the scale, ``(2 / a_h) sum_{b,i} eps delta_i / Z_i`` with ``delta_i = dO_i . O_i``.
+row ``Z = sum_t Z_t`` is the family's ``sum p + eps`` and ``O = sum_t O_t Z_t / Z``
+(``fb_combine_terms``, one pass).  The backward runs ``fb_born_bwd_term`` per term with the
+combined O and Z (the term's share of dQ, dK, dV) and forms the scale gradient from the closed
+form of a score homogeneous of degree 2 in the scale, ``(2 / a_h) sum_{b,i} eps delta_i / Z_i``
+with ``delta_i = dO_i . O_i`` (``fb_delta_terms``).  ``rot k`` and the adjoint rotation of its
+gradient are ``fb_rotate_halves``.
 """
 from __future__ import annotations
 
@@ -54,47 +56,71 @@ def _born_bwd_term(dout, q, k, v, out, z, scale, doc, is_causal, eps, window_siz
     return dq, dk, dv
 
 
-def _combine(terms):
-    """O = sum O_t Z_t / Z and Z = sum Z_t over terms [(O_t fp32, Z_t)]."""
-    z = terms[0][1].clone()
-    num = terms[0][0] * terms[0][1].unsqueeze(-1)
-    for o_t, z_t in terms[1:]:
-        z += z_t
-        num.addcmul_(o_t, z_t.unsqueeze(-1))
-    return num / z.unsqueeze(-1), z
+def _combine(terms, out: torch.Tensor, z: torch.Tensor) -> None:
+    """fb_combine_terms: out = sum O_t Z_t / sum Z_t, z = sum Z_t over terms [(O_t fp32, Z_t)];
+    out (B, H', T, D) and z (B, H', T) may be strided views."""
+    B, H, T, D = terms[0][0].shape
+    a = _lib.FbCombineArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim = B, H, T, D
+    a.n_terms = len(terms)
+    a.out_dtype = _DTYPE_CODE[out.dtype]
+    for i, (o_t, z_t) in enumerate(terms):
+        a.o[i], a.z[i] = _ptr(o_t), _ptr(z_t)
+    a.out, a.out_stride = _ptr(out), _strides(out)
+    a.z_out = _ptr(z)
+    a.z_stride = (ctypes.c_int64 * 3)(*z.stride())
+    with torch.cuda.device(out.device):
+        _lib.check(_lib.load().fb_combine_terms(ctypes.byref(a), _stream_handle(out.device)), "combine terms")
+
+
+def _rotate(b: torch.Tensor, a: Optional[torch.Tensor] = None, adjoint: bool = False) -> torch.Tensor:
+    """fb_rotate_halves: a + R b (adjoint: a + R^T b) per row of the last dimension."""
+    b = b.contiguous()
+    a = None if a is None else a.contiguous()  # held until the launch is enqueued
+    dst = torch.empty_like(b)
+    r = _lib.FbRotArgs()
+    r.rows, r.head_dim = b.numel() // b.shape[-1], b.shape[-1]
+    r.dtype, r.adjoint = _DTYPE_CODE[b.dtype], int(adjoint)
+    r.a = None if a is None else _ptr(a)
+    r.b, r.dst = _ptr(b), _ptr(dst)
+    with torch.cuda.device(b.device):
+        _lib.check(_lib.load().fb_rotate_halves(ctypes.byref(r), _stream_handle(b.device)), "rotate halves")
+    return dst
 
 
 def _scale_grad(dout, out, z, scale, eps, heads_of_row):
-    """(2 / a_h) sum eps delta_i / Z_i per scale entry; heads_of_row maps the (B, H', T) rows'
-    head axis to scale entries (identity for per-head scales)."""
-    delta = (dout.float() * out).sum(-1)                     # (B, H', T)
-    per_head = (eps * delta / z).sum(dim=(0, 2))             # (H',)
+    """(2 / a_e) sum eps delta_i / Z_i per scale entry e (fb_delta_terms gives the per-(b, h) sums;
+    heads_of_row maps the per-head sums onto scale entries)."""
+    B, H, T, D = out.shape
+    part = torch.empty((B, H), dtype=torch.float32, device=out.device)
+    a = _lib.FbDeltaArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim = B, H, T, D
+    a.dout_dtype, a.out_dtype = _DTYPE_CODE[dout.dtype], _DTYPE_CODE[out.dtype]
+    a.eps = float(eps)
+    a.dout, a.dout_stride = _ptr(dout), _strides(dout)
+    a.out, a.out_stride = _ptr(out), _strides(out)
+    a.z, a.part = _ptr(z), _ptr(part)
+    with torch.cuda.device(out.device):
+        _lib.check(_lib.load().fb_delta_terms(ctypes.byref(a), _stream_handle(out.device)), "scale gradient")
+    per_head = part.sum(dim=0)
     if scale.numel() == 1:
         return (2.0 / scale) * per_head.sum().reshape(1)
     return (2.0 / scale) * heads_of_row(per_head)
 
 
-def _rot(k: torch.Tensor) -> torch.Tensor:
-    half = k.shape[-1] // 2
-    return torch.cat((-k[..., half:], k[..., :half]), dim=-1)
-
-
-def _rot_t(g: torch.Tensor) -> torch.Tensor:
-    """Adjoint of _rot: the gradient for k of a gradient g for rot k."""
-    half = g.shape[-1] // 2
-    return torch.cat((g[..., half:], -g[..., :half]), dim=-1)
-
-
 class _ComplexPhaseBorn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, doc, is_causal, eps, window_size):
-        kr = _rot(k).contiguous()
+        kr = _rotate(k)
         terms = [_born_fwd(q, kk, v, scale, None, doc, is_causal, eps / 2, window_size, 0.0, False, False, True)
                  for kk in (k, kr)]
-        out, z = _combine(terms)
+        B, H, T, D = q.shape
+        out = torch.empty((B, H, T, D), dtype=v.dtype, device=v.device)
+        z = torch.empty((B, H, T), dtype=torch.float32, device=v.device)
+        _combine(terms, out, z)
         ctx.save_for_backward(q, k, kr, v, out, z, scale, doc)
         ctx.cfg = (is_causal, eps, window_size)
-        return out.to(v.dtype)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
@@ -103,9 +129,9 @@ class _ComplexPhaseBorn(torch.autograd.Function):
         dout = _prep(dout.to(v.dtype))
         dq1, dk1, dv1 = _born_bwd_term(dout, q, k, v, out, z, scale, doc, is_causal, eps / 2, window_size)
         dq2, dkr, dv2 = _born_bwd_term(dout, q, kr, v, out, z, scale, doc, is_causal, eps / 2, window_size)
-        dk = dk1 + _rot_t(dkr)
+        dk = _rotate(dkr, dk1, adjoint=True)
         dscale = _scale_grad(dout, out, z, scale, eps, lambda x: x)
-        return dq1 + dq2, dk, dv1 + dv2, dscale, None, None, None, None
+        return dq1.add_(dq2), dk, dv1.add_(dv2), dscale, None, None, None, None
 
 
 def complex_phase_born_attention(
@@ -144,19 +170,18 @@ def complex_phase_born_attention(
 class _PairedHeadsBorn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, doc, is_causal, eps, window_size):
-        P = q.shape[1] // 2
+        B, H, T, D = q.shape
+        P = H // 2
         half = lambda x, a: x[:, a * P:(a + 1) * P]  # noqa: E731  head half a: (B, P, T, D) view
-        outs, zs = [], []
+        out = torch.empty((B, H, T, D), dtype=v.dtype, device=v.device)
+        z = torch.empty((B, H, T), dtype=torch.float32, device=v.device)
         for a in (0, 1):
             terms = [_born_fwd(half(q, a), half(k, b), half(v, b), scale, None, doc, is_causal, eps / 2,
                                window_size, 0.0, False, False, True) for b in (0, 1)]
-            o_a, z_a = _combine(terms)
-            outs.append(o_a)
-            zs.append(z_a)
-        out, z = torch.cat(outs, dim=1), torch.cat(zs, dim=1)
+            _combine(terms, half(out, a), half(z, a))
         ctx.save_for_backward(q, k, v, out, z, scale, doc)
         ctx.cfg = (is_causal, eps, window_size)
-        return out.to(v.dtype)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
@@ -165,18 +190,18 @@ class _PairedHeadsBorn(torch.autograd.Function):
         P = q.shape[1] // 2
         dout = _prep(dout.to(v.dtype))
         half = lambda x, a: x[:, a * P:(a + 1) * P]  # noqa: E731
-        dq, dk, dv = torch.zeros_like(q, dtype=torch.float32), torch.zeros_like(k, dtype=torch.float32), \
-            torch.zeros_like(v, dtype=torch.float32)
+        g = {}
         for a in (0, 1):
-            o_a, z_a = out[:, a * P:(a + 1) * P], z[:, a * P:(a + 1) * P].contiguous()
             for b in (0, 1):
-                gq, gk, gv = _born_bwd_term(half(dout, a), half(q, a), half(k, b), half(v, b), o_a, z_a, scale, doc,
-                                            is_causal, eps / 2, window_size)
-                half(dq, a).add_(gq)
-                half(dk, b).add_(gk)
-                half(dv, b).add_(gv)
+                g[a, b] = _born_bwd_term(half(dout, a), half(q, a), half(k, b), half(v, b), half(out, a),
+                                         half(z, a).contiguous(), scale, doc, is_causal, eps / 2, window_size)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        for x in (0, 1):  # query half x gathers over key halves; key half x over query halves
+            torch.add(g[x, 0][0], g[x, 1][0], out=half(dq, x))
+            torch.add(g[0, x][1], g[1, x][1], out=half(dk, x))
+            torch.add(g[0, x][2], g[1, x][2], out=half(dv, x))
         dscale = _scale_grad(dout, out, z, scale, eps, lambda x: x[:P] + x[P:])
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dscale, None, None, None, None
+        return dq, dk, dv, dscale, None, None, None, None
 
 
 def paired_heads_born_attention(

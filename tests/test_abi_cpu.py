@@ -136,3 +136,16 @@ def test_path_selection_is_host_only():
     assert lib.fb_born_fwd(ctypes.byref(a), None) == _lib.FB_ERR_UNSUPPORTED
     a.path = _lib.FB_PATH_GENERAL
     assert lib.fb_select_path(ctypes.byref(a), 1) == _lib.FB_PATH_GENERAL
+
+
+def test_cross_entropy_validation_without_gpu():
+    lib = _lib.load()
+    a = _lib.FbXentArgs()
+    a.rows, a.vocab, a.ld = 4, 64, 64
+    a.logits = a.targets = a.lse = a.loss = 0x10000  # never dereferenced: validation fails first
+    for field, val, code in (("vocab", 63, _lib.FB_ERR_SHAPE), ("ld", 32, _lib.FB_ERR_SHAPE),
+                             ("logits", None, _lib.FB_ERR_ARG), ("logits", 0x10008, _lib.FB_ERR_ALIGN)):
+        b = _lib.FbXentArgs.from_buffer_copy(a)
+        setattr(b, field, val)
+        assert lib.fb_xent_fwd(ctypes.byref(b), None) == code, field
+    assert lib.fb_xent_bwd(ctypes.byref(a), None) == _lib.FB_ERR_ARG  # grad / gscale missing
