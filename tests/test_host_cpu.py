@@ -86,3 +86,16 @@ def test_prologue_ops_raise_on_cpu_and_check_shapes():
         qkv_rope_l2norm(torch.zeros(1, 8, 3 * 64), cos, sin, 1)
     with pytest.raises(RuntimeError, match="CUDA"):
         l2_normalize(torch.zeros(2, 8))
+
+
+def test_family_and_loss_ops_raise_on_cpu():
+    """No CPU fallback: the families and the loss refuse CPU tensors, and check their shapes."""
+    from quantumdlblocks_b200 import complex_phase_born_attention, paired_heads_born_attention
+    from quantumdlblocks_b200.kernels.xent import cross_entropy
+
+    x = torch.zeros(1, 2, 8, 16)
+    for fn in (complex_phase_born_attention, paired_heads_born_attention):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            fn(x, x, x, 4.0)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cross_entropy(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int64))
