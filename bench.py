@@ -562,9 +562,10 @@ def run_gpt(args, rank: int, world: int, dev: torch.device) -> dict:
 def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -> None:
     """--mode prologue: the attention layer's fused operand prologue at the C5 layer shape
     (B=16, T=1024, 16 heads x 64, bf16 projection, fp32 residual stream): qkv_prologue forward and
-    backward and the row L2 normalisation forward and backward, each timed with CUDA events after
-    an L2 flush, against the HBM roofline (algorithmic bytes: every input element read once, every
-    output element written once)."""
+    backward and the row L2 normalisation forward and backward, and the GPT loss (fused
+    cross-entropy over 16,384 x 50,304 bf16 logits) forward and backward, each timed with CUDA
+    events after an L2 flush, against the HBM roofline (algorithmic bytes: every input element read
+    once, every output element written once)."""
     from quantumdlblocks_b200.kernels import flash_born as fbm
     from quantumdlblocks_b200.kernels.prologue import (_l2norm_rows, _l2norm_rows_bwd, _qkv_prologue,
                                                        _qkv_prologue_bwd, rope_tables)
@@ -584,6 +585,26 @@ def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -
         "l2norm_rows_fwd": (lambda: _l2norm_rows(x, 1e-12), 2 * x.numel() * 4),
         "l2norm_rows_bwd": (lambda: _l2norm_rows_bwd(x, dy, 1e-12), 3 * x.numel() * 4),
     }
+    # the GPT loss at the C5 shape: 16,384 rows of 50,304 bf16 logits (fwd reads them once; bwd
+    # reads them and writes the gradient), through the C ABI with preallocated buffers
+    import ctypes
+
+    from quantumdlblocks_b200 import _lib
+
+    rows, vocab = B * T, 50304
+    logits = torch.randn(rows, vocab, generator=g, device=dev).to(torch.bfloat16)
+    tgt = torch.randint(0, 50257, (rows,), generator=g, device=dev)
+    lse, loss = (torch.empty(rows, dtype=torch.float32, device=dev) for _ in range(2))
+    dlog = torch.empty_like(logits)
+    gs = torch.ones(1, dtype=torch.float32, device=dev)
+    xa = _lib.FbXentArgs()
+    xa.rows, xa.vocab, xa.ld = rows, vocab, vocab
+    xa.logits, xa.targets, xa.lse, xa.loss = logits.data_ptr(), tgt.data_ptr(), lse.data_ptr(), loss.data_ptr()
+    xa.grad, xa.gscale = dlog.data_ptr(), gs.data_ptr()
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    cases["xent_fwd"] = (lambda: _lib.check(lib.fb_xent_fwd(ctypes.byref(xa), stream), "xent"), rows * vocab * 2)
+    cases["xent_bwd"] = (lambda: _lib.check(lib.fb_xent_bwd(ctypes.byref(xa), stream), "xent"), rows * vocab * 4)
     peaks, src = load_peaks()
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     res = {}

@@ -58,19 +58,32 @@ __global__ void __launch_bounds__(kXentThreads) xent_fwd_kernel(const XentParams
   const __nv_bfloat16* x = p.logits + row * p.ld;
   const int nchunk = p.V / 8;
   float m = -INFINITY, s = 0.f;
-  for (int c = threadIdx.x; c < nchunk; c += kXentThreads) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(x + 8 * c), f);
-    float cm = f[0];
+  // kUnroll chunks are requested before any is used, so each thread keeps 64 bytes in flight;
+  // chunks past the row read as -inf (bf16 0xFF80), which adds nothing
+  constexpr int kUnroll = 4;
+  for (int c0 = threadIdx.x; c0 < nchunk; c0 += kUnroll * kXentThreads) {
+    uint4 w[kUnroll];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) cm = fmaxf(cm, f[i]);
-    if (cm == -INFINITY) continue;  // a chunk of masked columns
-    if (cm > m) {
-      s = s * __expf(m - cm);
-      m = cm;
+    for (int u = 0; u < kUnroll; ++u) {
+      const int c = c0 + u * kXentThreads;
+      w[u] = c < nchunk ? __ldg(reinterpret_cast<const uint4*>(x + 8 * c))
+                        : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s += __expf(f[i] - m);
+    for (int u = 0; u < kUnroll; ++u) {
+      float f[8];
+      unpack8(w[u], f);
+      float cm = f[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) cm = fmaxf(cm, f[i]);
+      if (cm == -INFINITY) continue;  // a chunk of masked columns
+      if (cm > m) {
+        s = s * __expf(m - cm);
+        m = cm;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += __expf(f[i] - m);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) merge(m, s, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, s, o));
