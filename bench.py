@@ -563,7 +563,8 @@ def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -
     """--mode prologue: the attention layer's fused operand prologue at the C5 layer shape
     (B=16, T=1024, 16 heads x 64, bf16 projection, fp32 residual stream): qkv_prologue forward and
     backward and the row L2 normalisation forward and backward, and the GPT loss (fused
-    cross-entropy over 16,384 x 50,304 bf16 logits) forward and backward, each timed with CUDA
+    cross-entropy over 16,384 x 50,304 bf16 logits) forward and backward, the head epilogue (gated
+    XSA, output gate, head merge) forward and forward + backward, each timed with CUDA
     events after an L2 flush, against the HBM roofline (algorithmic bytes: every input element read
     once, every output element written once)."""
     from quantumdlblocks_b200.kernels import flash_born as fbm
@@ -605,6 +606,26 @@ def run_prologue_mode(args, rank: int, flush: torch.Tensor, dev: torch.device) -
     stream = torch.cuda.current_stream(dev).cuda_stream
     cases["xent_fwd"] = (lambda: _lib.check(lib.fb_xent_fwd(ctypes.byref(xa), stream), "xent"), rows * vocab * 2)
     cases["xent_bwd"] = (lambda: _lib.check(lib.fb_xent_bwd(ctypes.byref(xa), stream), "xent"), rows * vocab * 4)
+    # the layer's head epilogue (gated XSA + output gate + head merge) at the C5 layer shape
+    from quantumdlblocks_b200.kernels.epilogue import finalize_heads
+
+    eo = dq.detach().clone().requires_grad_(True)
+    ev = dk.detach().clone().requires_grad_(True)
+    ea = torch.zeros(H, device=dev).requires_grad_(True)
+    ex = x.detach().clone().requires_grad_(True)
+    ew, eb = torch.zeros(H, 6, device=dev).requires_grad_(True), torch.zeros(H, device=dev).requires_grad_(True)
+    edy = torch.randn(B, T, D, generator=g, device=dev).to(torch.bfloat16)
+    hb = eo.numel() * 2
+
+    def epi_fwd():
+        with torch.no_grad():
+            finalize_heads(eo, ev, ea, ex, ew, eb)
+
+    def epi_step():
+        torch.autograd.grad(finalize_heads(eo, ev, ea, ex, ew, eb), (eo, ev, ea, ex, ew, eb), edy)
+
+    cases["heads_epilogue_fwd"] = (epi_fwd, 3 * hb)  # read O, V; write Y
+    cases["heads_epilogue_fwd_bwd"] = (epi_step, 3 * hb + 5 * hb)  # + read dY, O, V; write dO, dV
     peaks, src = load_peaks()
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     res = {}

@@ -190,6 +190,42 @@ FB_API int fb_rotate_halves(const fb_rot_args* args, void* stream);
 FB_API int fb_combine_terms(const fb_combine_args* args, void* stream);
 FB_API int fb_delta_terms(const fb_delta_args* args, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * The layer's head epilogue (ABI version 4), _finalize_heads of the reference
+ * (layers/attention.py:478-493) up to out_proj:
+ *   r = y - tanh(alpha_h) (y . v) / (|v|^2 + eps) v      gated XSA (layers/mudd_and_gates.py:45-61),
+ *                                                        when xsa_alpha is given
+ *   g = 2 sigmoid(b_h + sum_k x[b, t, k] W[h, k])        input gate (mudd_and_gates.py:17-42), when
+ *                                                        gate_x is given (else g = 1)
+ *   Y[b, t, h hd + i] = g r_i                            heads merged for out_proj
+ * o (the attention output) and v are (B, H, T, hd) with any 16-byte aligned strides (unit inner
+ * stride); Y and dY are (B, T, H hd) contiguous; gate_x (B, T, gate_channels <= 8), gate_w
+ * (H, gate_channels), gate_b and xsa_alpha (H) are fp32 contiguous; dtype FB_BF16 or FB_F32 for
+ * o, v, Y and the gradients; hd 32, 64 or 128.  The backward writes grad_o and grad_v (B, H, T, hd)
+ * contiguous and, per (b, t, h), dalpha = d/d alpha_h and du = d/d (gate pre-activation), whose
+ * sums over rows (and products with gate_x) give the parameter gradients.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct fb_heads_args {
+  int32_t batch, heads, seq_len, head_dim;
+  int32_t dtype;
+  float eps;
+  const void* o; int64_t o_stride[4];
+  const void* v; int64_t v_stride[4];
+  const float* xsa_alpha;
+  const float* gate_x; int32_t gate_channels;
+  const float* gate_w;
+  const float* gate_b;
+  void* y;          /* forward output */
+  const void* dy;   /* backward input */
+  void* grad_o;     /* backward outputs */
+  void* grad_v;
+  float* dalpha;
+  float* du;
+} fb_heads_args;
+
+FB_API int fb_heads_epilogue_fwd(const fb_heads_args* args, void* stream);
+FB_API int fb_heads_epilogue_bwd(const fb_heads_args* args, void* stream);
+
 /* Plain flash-Born backward that allocates nothing and takes no workspace: its scratch is a
  * fixed FB_STATIC_SCRATCH_BYTES device array inside the library (one per GPU, held from the
  * first call on that GPU until exit).  For callers that cannot allocate device memory (a host

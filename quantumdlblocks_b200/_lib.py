@@ -112,6 +112,18 @@ class FbDeltaArgs(ctypes.Structure):
     ]
 
 
+class FbHeadsArgs(ctypes.Structure):
+    """Mirror of ``fb_heads_args`` (the layer's head epilogue)."""
+    _fields_ = [
+        ("batch", ctypes.c_int32), ("heads", ctypes.c_int32), ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("o", ctypes.c_void_p), ("o_stride", _I64x4), ("v", ctypes.c_void_p), ("v_stride", _I64x4),
+        ("xsa_alpha", ctypes.c_void_p), ("gate_x", ctypes.c_void_p), ("gate_channels", ctypes.c_int32),
+        ("gate_w", ctypes.c_void_p), ("gate_b", ctypes.c_void_p), ("y", ctypes.c_void_p), ("dy", ctypes.c_void_p),
+        ("grad_o", ctypes.c_void_p), ("grad_v", ctypes.c_void_p), ("dalpha", ctypes.c_void_p), ("du", ctypes.c_void_p),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 _PARGS = ctypes.POINTER(FbAttnArgs)
 _PQKV = ctypes.POINTER(FbQkvArgs)
@@ -137,6 +149,8 @@ SIGNATURES = {
     "fb_l2norm_rows_fwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
     "fb_l2norm_rows_bwd": (ctypes.c_int, [_PROWS, ctypes.c_void_p]),
     "fb_xent_fwd": (ctypes.c_int, [_PXENT, ctypes.c_void_p]),
+    "fb_heads_epilogue_fwd": (ctypes.c_int, [ctypes.POINTER(FbHeadsArgs), ctypes.c_void_p]),
+    "fb_heads_epilogue_bwd": (ctypes.c_int, [ctypes.POINTER(FbHeadsArgs), ctypes.c_void_p]),
     "fb_rotate_halves": (ctypes.c_int, [ctypes.POINTER(FbRotArgs), ctypes.c_void_p]),
     "fb_combine_terms": (ctypes.c_int, [ctypes.POINTER(FbCombineArgs), ctypes.c_void_p]),
     "fb_delta_terms": (ctypes.c_int, [ctypes.POINTER(FbDeltaArgs), ctypes.c_void_p]),

@@ -149,3 +149,24 @@ def test_cross_entropy_validation_without_gpu():
         setattr(b, field, val)
         assert lib.fb_xent_fwd(ctypes.byref(b), None) == code, field
     assert lib.fb_xent_bwd(ctypes.byref(a), None) == _lib.FB_ERR_ARG  # grad / gscale missing
+
+
+def test_heads_epilogue_validation_without_gpu():
+    lib = _lib.load()
+    a = _lib.FbHeadsArgs()
+    a.batch, a.heads, a.seq_len, a.head_dim, a.dtype = 1, 2, 4, 64, _lib.FB_BF16
+    a.o, a.y = 0x10000, 0x10000  # never dereferenced: validation fails first
+    a.o_stride = _lib._I64x4(512, 256, 64, 1)
+    b = _lib.FbHeadsArgs.from_buffer_copy(a)
+    b.head_dim = 48
+    assert lib.fb_heads_epilogue_fwd(ctypes.byref(b), None) == _lib.FB_ERR_SHAPE
+    b = _lib.FbHeadsArgs.from_buffer_copy(a)
+    b.xsa_alpha = 0x10000  # XSA without v
+    assert lib.fb_heads_epilogue_fwd(ctypes.byref(b), None) == _lib.FB_ERR_ARG
+    b = _lib.FbHeadsArgs.from_buffer_copy(a)
+    b.o_stride = _lib._I64x4(512, 256, 63, 1)
+    assert lib.fb_heads_epilogue_fwd(ctypes.byref(b), None) == _lib.FB_ERR_ALIGN
+    b = _lib.FbHeadsArgs.from_buffer_copy(a)
+    b.gate_x, b.gate_channels = 0x10000, 9  # more gate channels than the kernel holds
+    assert lib.fb_heads_epilogue_fwd(ctypes.byref(b), None) == _lib.FB_ERR_ARG
+    assert lib.fb_heads_epilogue_bwd(ctypes.byref(a), None) == _lib.FB_ERR_ARG  # dy / grad_o missing

@@ -99,3 +99,10 @@ def test_family_and_loss_ops_raise_on_cpu():
             fn(x, x, x, 4.0)
     with pytest.raises(RuntimeError, match="CUDA"):
         cross_entropy(torch.zeros(4, 64, dtype=torch.bfloat16), torch.zeros(4, dtype=torch.int64))
+
+
+def test_finalize_heads_raises_on_cpu():
+    from quantumdlblocks_b200.kernels.epilogue import finalize_heads
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        finalize_heads(torch.zeros(1, 2, 4, 64))
