@@ -160,8 +160,28 @@ __host__ __device__ inline int doc_blocks(int T) { return (T + kDocBlock - 1) / 
 struct DocRanges {
   const int2* qr;
   const int2* kr;
+  const int2* mm;  // per 64-row block (min, max) document id
   int nblk;
 };
+
+// True when the query rows [m0, m0 + qrows) and key rows [n0, n0 + krows) all carry one and the
+// same document id (every block's min equals its max and the blocks agree): the document mask is
+// then all-true on the tile and only the causal / window / length conditions remain.
+__device__ __forceinline__ bool doc_single(const int2* mm, int nblk, int b, int m0, int qrows, int n0, int krows) {
+  const int2* m = mm + (int64_t)b * nblk;
+  const int2 a = __ldg(&m[min(m0 / kDocBlock, nblk - 1)]);
+  if (a.x != a.y) return false;
+  bool one = true;
+  for (int x = m0 / kDocBlock; x <= min((m0 + qrows - 1) / kDocBlock, nblk - 1); ++x) {
+    const int2 v = __ldg(&m[x]);
+    one = one && v.x == a.x && v.y == a.x;
+  }
+  for (int x = n0 / kDocBlock; x <= min((n0 + krows - 1) / kDocBlock, nblk - 1); ++x) {
+    const int2 v = __ldg(&m[x]);
+    one = one && v.x == a.x && v.y == a.x;
+  }
+  return one;
+}
 
 // Narrows the other side's row range [lo, hi) of a tile whose own rows are [row0, row0 + rows) to
 // the blocks that can share a document with those rows; no-op without document ids (r == null).

@@ -76,7 +76,7 @@ size_t doc_ranges_bytes(const Problem& p) {
 }
 
 int doc_ranges(const Problem& p, cudaStream_t s, void* ws, DocRanges* out) {
-  out->qr = out->kr = nullptr;
+  out->qr = out->kr = out->mm = nullptr;
   out->nblk = doc_blocks(p.T);
   if (p.doc == nullptr) return FB_OK;
   const size_t n = align256((size_t)p.B * out->nblk * sizeof(int2));
@@ -93,6 +93,7 @@ int doc_ranges(const Problem& p, cudaStream_t s, void* ws, DocRanges* out) {
   }
   out->qr = qr;
   out->kr = kr;
+  out->mm = mm;
   return FB_OK;
 }
 

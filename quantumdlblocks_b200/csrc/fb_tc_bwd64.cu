@@ -100,6 +100,7 @@ struct BwdParams {
   int n_kv, n_items;
   int map3;            // tensor maps address (b, h) as one merged dimension
   const int2* doc_kr;  // document spans of the key blocks (null without document ids)
+  const int2* doc_mm;  // per-block (min, max) document ids
   int nblk;
   int* status;
 };
@@ -484,11 +485,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         }
+        // with document ids: every row of the tile in one document?  (read before the waits, so
+        // the loads' latency hides behind them)
+        bool one_doc = !kHasDoc;
+        if constexpr (kHasDoc) one_doc = doc_single(p.doc_mm, p.nblk, it.b, m0, kBM, n0, kBN);
         ok = __all_sync(0xffffffffu, mbar_wait(&vec_full[gg % kQS], (gg / kQS) & 1, wc, 32));
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sdp_full[sb], (gg >> 1) & 1, wc, 30));
         if (!ok) break;
         tc_fence_after();
-        const bool full = !kHasDoc && (!p.causal || m0 >= n0 + kBN - 1) &&
+        const bool full = one_doc && (!p.causal || m0 >= n0 + kBN - 1) &&
                           (p.window <= 0 || (m0 + kBM - 1) - n0 < p.window) && (m0 + kBM <= p.T) &&
                           (n0 + kBN <= p.T);
         const float* dl = vdlz + (gg % kQS) * kBM;
@@ -951,6 +956,7 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   const int drc = doc_ranges(pr, s, ws + w.docs, &dr);
   if (drc != FB_OK) return drc;
   bp.doc_kr = dr.kr;
+  bp.doc_mm = dr.mm;
   bp.nblk = dr.nblk;
 
   CUtensorMap mdq;

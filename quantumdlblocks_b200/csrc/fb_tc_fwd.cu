@@ -95,6 +95,7 @@ struct FwdParams {
   const int32_t* doc;
   int64_t doc_s0, doc_s1;
   const int2* doc_qr;  // document spans of the query blocks (null without document ids)
+  const int2* doc_mm;  // per-block (min, max) document ids
   int nblk;
   void* out;
   int64_t o_s0, o_s1, o_s2;
@@ -376,11 +377,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         }
+        // with document ids: every row of the tile in one document?  (read before the wait, so the
+        // loads' latency hides behind it)
+        bool one_doc = !kHasDoc;
+        if constexpr (kHasDoc) one_doc = doc_single(p.doc_mm, p.nblk, it.b, it.m0, kBM, n0, kBN);
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[wg], (gg >> 1) & 1, wc, 8));  // warp-uniform
         if (!ok) break;
         tc_fence_after();
-        // whole tile valid?  (below the causal diagonal, inside the window, inside T, no doc ids)
-        const bool full = !kHasDoc && (!p.causal || n0 + kBN - 1 <= it.m0) &&
+        // whole tile valid?  (below the causal diagonal, inside the window, inside T, and with
+        // document ids every row of the tile in one document)
+        const bool full = one_doc && (!p.causal || n0 + kBN - 1 <= it.m0) &&
                           (p.window <= 0 || (it.m0 + kBM - 1) - n0 < p.window) && (n0 + kBN <= p.T);
         if (gg >= 2) {  // P[wg] is free once O += P_{gg-2} V_{gg-2} has completed
           ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[wg], ((gg - 2) >> 1) & 1, wc, 9));
@@ -388,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // causal diagonal tile (the item's own 128 keys): chunk c of warp lg is entirely valid for
         // c < lg, entirely masked for c > lg, and valid for column e <= lane when c == lg
-        const bool diag = !full && !kHasDoc && p.causal && p.window <= 0 && n0 == it.m0;
+        const bool diag = !full && one_doc && p.causal && p.window <= 0 && n0 == it.m0;
         if (full) {
           // four 32-column chunks, software pipelined: the TMEM load of chunk c+1 is in flight
           // while chunk c is turned into P (the loads would otherwise expose their latency)
@@ -598,6 +604,7 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   const int drc = doc_ranges(pr, s, pr.ws, &dr);  // workspace of doc_ranges_bytes(pr) bytes
   if (drc != FB_OK) return drc;
   fp.doc_qr = dr.qr;
+  fp.doc_mm = dr.mm;
   fp.nblk = dr.nblk;
   fp.out = const_cast<void*>(pr.o.ptr);
   fp.o_s0 = pr.o.s[0]; fp.o_s1 = pr.o.s[1]; fp.o_s2 = pr.o.s[2];

@@ -41,6 +41,9 @@ CASES = [
     (1, 2, 700, 128, False, 260, None),
     (2, 2, 900, 64, True, 0, 120.0),
     (1, 2, 640, 128, True, 0, 60.0),
+    # long documents: most tiles lie inside one document and take the unmasked fast path
+    (2, 2, 1500, 64, True, 0, 600.0),
+    (1, 2, 1100, 128, True, 0, 500.0),
 ]
 
 
