@@ -153,9 +153,10 @@ FB_API int fb_born_bwd_term(const fb_attn_args* args, void* stream);
  *   fb_combine_terms   O = sum_t O_t Z_t / sum_t Z_t, Z = sum_t Z_t over n_terms (1..4) term outputs
  *                      O_t (B, H, T, D) fp32 contiguous (16-byte aligned) and Z_t (B, H, T) fp32
  *                      contiguous; O written as out_dtype through out_stride, Z through z_stride
- *   fb_delta_terms     part[b, h] = sum_t eps (dO . O) / Z over (b, h)'s rows: the family's scale
- *                      gradient is (2 / scale) times the sum of part over the rows that scale
- *                      entry serves (Z contiguous (B, H, T); part (B, H) fp32) */
+ *   fb_delta_terms     part[b, h, c] = sum_t eps (dO . O) / Z over rows t of 64-row chunk c of
+ *                      (b, h): the family's scale gradient is (2 / scale) times the sum of part
+ *                      over the rows that scale entry serves (Z contiguous (B, H, T); part
+ *                      (B, H, ceil(T / 64)) fp32) */
 typedef struct fb_rot_args {
   int64_t rows;
   int32_t head_dim;

@@ -89,10 +89,10 @@ def _rotate(b: torch.Tensor, a: Optional[torch.Tensor] = None, adjoint: bool = F
 
 
 def _scale_grad(dout, out, z, scale, eps, heads_of_row):
-    """(2 / a_e) sum eps delta_i / Z_i per scale entry e (fb_delta_terms gives the per-(b, h) sums;
+    """(2 / a_e) sum eps delta_i / Z_i per scale entry e (fb_delta_terms gives per-(b, h, 64-row) sums;
     heads_of_row maps the per-head sums onto scale entries)."""
     B, H, T, D = out.shape
-    part = torch.empty((B, H), dtype=torch.float32, device=out.device)
+    part = torch.empty((B, H, (T + 63) // 64), dtype=torch.float32, device=out.device)
     a = _lib.FbDeltaArgs()
     a.batch, a.heads, a.seq_len, a.head_dim = B, H, T, D
     a.dout_dtype, a.out_dtype = _DTYPE_CODE[dout.dtype], _DTYPE_CODE[out.dtype]
@@ -102,7 +102,7 @@ def _scale_grad(dout, out, z, scale, eps, heads_of_row):
     a.z, a.part = _ptr(z), _ptr(part)
     with torch.cuda.device(out.device):
         _lib.check(_lib.load().fb_delta_terms(ctypes.byref(a), _stream_handle(out.device)), "scale gradient")
-    per_head = part.sum(dim=0)
+    per_head = part.sum(dim=(0, 2))
     if scale.numel() == 1:
         return (2.0 / scale) * per_head.sum().reshape(1)
     return (2.0 / scale) * heads_of_row(per_head)
