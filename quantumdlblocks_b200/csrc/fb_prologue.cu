@@ -288,6 +288,66 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32) l2norm_rows_bwd_kernel(co
   }
 }
 
+// Rows of at most 32 N R elements: each lane keeps its R chunks of the row in registers (packed),
+// so the row is read once and all its loads are in flight together.
+template <typename T, int R>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32) l2norm_rows_reg_kernel(const RowsParams p, bool bwd) {
+  constexpr int N = Chunk<T>::N;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= p.rows) return;  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const T* x = static_cast<const T*>(p.x) + row * p.cols;
+  uint4 rx[R], rg[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = (j * 32 + lane) * N;
+    rx[j] = c < p.cols ? *reinterpret_cast<const uint4*>(x + c) : make_uint4(0u, 0u, 0u, 0u);
+    if (bwd) rg[j] = c < p.cols ? *reinterpret_cast<const uint4*>(static_cast<const T*>(p.dy) + row * p.cols + c)
+                                : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float ss = 0.f, xd = 0.f;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    float f[N], g[N];
+    Chunk<T>::unpack(rx[j], f);
+    if (bwd) Chunk<T>::unpack(rg[j], g);
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      ss = fmaf(f[i], f[i], ss);
+      if (bwd) xd = fmaf(f[i], g[i], xd);
+    }
+  }
+  const float r = rsqrtf(warp_sum(ss) + p.eps);
+  const float k3 = bwd ? r * r * r * warp_sum(xd) : 0.f;  // dx = r dy - x r^3 (x . dy)
+  T* out = static_cast<T*>(bwd ? p.dx : p.y) + row * p.cols;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = (j * 32 + lane) * N;
+    if (c >= p.cols) continue;
+    float f[N], g[N];
+    Chunk<T>::unpack(rx[j], f);
+    if (bwd) {
+      Chunk<T>::unpack(rg[j], g);
+#pragma unroll
+      for (int i = 0; i < N; ++i) g[i] = fmaf(r, g[i], -f[i] * k3);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) g[i] = f[i] * r;
+    }
+    Chunk<T>::store(out + c, g);
+  }
+}
+
+template <typename T>
+bool launch_rows_reg(const RowsParams& p, bool bwd, unsigned grid, cudaStream_t s) {
+  const int chunks = (p.cols + 32 * Chunk<T>::N - 1) / (32 * Chunk<T>::N);  // per lane
+  if (chunks <= 2) l2norm_rows_reg_kernel<T, 2><<<grid, kWarpsPerBlock * 32, 0, s>>>(p, bwd);
+  else if (chunks <= 4) l2norm_rows_reg_kernel<T, 4><<<grid, kWarpsPerBlock * 32, 0, s>>>(p, bwd);
+  else if (chunks <= 8) l2norm_rows_reg_kernel<T, 8><<<grid, kWarpsPerBlock * 32, 0, s>>>(p, bwd);
+  else return false;
+  return true;
+}
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 int finish_launch(int n) {
@@ -349,6 +409,10 @@ int l2norm_rows(const fb_rows_args* a, void* stream, bool backward) {
   RowsParams p{a->rows, a->cols, a->eps, a->x, a->y, a->dy, a->dx};
   const unsigned grid = (unsigned)((a->rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // rows of up to 8 chunks per lane stay in registers; longer rows take the two-pass kernels
+  const bool in_regs = a->dtype == FB_BF16 ? launch_rows_reg<__nv_bfloat16>(p, backward, grid, s)
+                                           : launch_rows_reg<float>(p, backward, grid, s);
+  if (in_regs) return finish_launch(1);
   if (backward) {
     if (a->dtype == FB_BF16)
       l2norm_rows_bwd_kernel<__nv_bfloat16><<<grid, kWarpsPerBlock * 32, 0, s>>>(p);
