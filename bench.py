@@ -6,9 +6,13 @@
 One step = one forward + backward of Born attention over one batch of synthetic inputs resident
 in HBM (C2: B=8, H=16, N=2048, d=64, bf16, causal, per-head scale 8, eps 1e-12; Q, K, V from
 torch seed 0, dO from seed 1, drawn in fp32 then cast).  With N GPUs (one process per GPU,
-launched by torch.distributed.run) every rank runs its own C2-sized slice of a global batch of
-8N sequences (weak scaling; the (batch, head) units are independent, so there is no collective
-on the data path); value = all ranks' FLOPs / the slowest rank's device time.
+launched by torch.distributed.run) the one problem is split over the ranks (strong scaling):
+every rank takes a rectangle of its (batch, head) units from sharding.plan_shards -- C2's 128
+units become 64 / 32 / 16 per GPU at N = 2 / 4 / 8 (heads split), C3's 32 heads 4 per GPU at
+N = 8 -- and runs it with no collective on the data path (the units are independent); value =
+the problem's FLOPs / the slowest rank's device time.  ``--weak`` gives every rank a whole
+problem of its own instead (weak scaling); the strong run also reports that figure under
+``"weak_scaling"``.
 
 FLOPs are algorithmic: 14 d per valid (query, key) pair (forward QK^T and PV, backward S
 recompute, dP, dV, dK, dQ), elementwise work not counted.
@@ -27,7 +31,6 @@ import argparse
 import json
 import math
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -57,19 +60,17 @@ WORKLOADS = {
 }
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernel,
+# from an ncu capture of a named build: (bytes, source).  A static figure: a rebuilt kernel keeps
+# reporting it until it is profiled again, which is why its source names the profiled build.
+PROFILED_TRAFFIC = {
+    ("c2", "bwd"): (294.9e6, "static: ncu capture of tc_bwd_kernel at C2, build 6513c74"),
+}
+
+
 def profiled_traffic(workload: str, kernel: str):
-    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary
-    (profiles/tc_{fwd,bwd}_kernel_c2.md, line 'traffic X MB per launch'); None when the summary
-    does not cover this workload."""
-    if workload != "c2":
-        return None
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", f"tc_{kernel}_kernel_c2.md")
-    try:
-        text = open(path).read()
-    except OSError:
-        return None
-    m = re.search(r"traffic ([0-9.]+) MB per launch", text)
-    return float(m.group(1)) * 1e6 if m else None
+    """(bytes per launch, source) of the dominant kernel from PROFILED_TRAFFIC, or (None, reason)."""
+    return PROFILED_TRAFFIC.get((workload, kernel), (None, "not profiled for this workload"))
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -239,11 +240,12 @@ def run_reference_arm(args, rank: int, world: int) -> None:
         "warmup": args.warmup,
         "ms_per_step": 1e3 * secs / args.steps,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if args.weak else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": desc, "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D},
+        "config": {"workload": desc, "global_batch": B * world if args.weak else B, "seq_len": N, "heads": H,
+                   "head_dim": D},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": f"{units_total} whole (batch, head) units of {args.workload} (N={N}, d={D}), "
                                    f"{flops_unit / 1e9:.2f} GFLOP each, fp32, torch eager restatement of "
@@ -272,17 +274,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             dist.barrier()
 
     B, H, N, D, causal, desc = WORKLOADS[args.workload]
-    qc, kc, vc, doc_c, doc_np, scale_val = None, None, None, None, None, None
-    q_cpu, k_cpu, v_cpu, do_cpu, doc_np, scale_val = make_inputs(args.workload, rank)
+    split = world > 1 and not args.weak
+    # strong scaling (default with N > 1 ranks): every rank takes its shard of the one BASELINE
+    # problem (rank 0's inputs), a rectangle of (batch, head) units from sharding.plan_shards,
+    # held contiguously on its GPU; weak scaling: every rank runs a whole problem of its own
+    q_cpu, k_cpu, v_cpu, do_cpu, doc_np, scale_val = make_inputs(args.workload, 0 if split else rank)
+    pairs_full = valid_pairs(args.workload, B, H, N, doc_np)
+    shard = None
+    if split:
+        from quantumdlblocks_b200.sharding import plan_shards
+
+        shard = plan_shards(B, H, N, world, is_causal=causal, doc_ids=doc_np)[rank]
+        bs, hs = slice(shard.b0, shard.b1), slice(shard.h0, shard.h1)
+        q_cpu, k_cpu, v_cpu, do_cpu = (x[bs, hs].contiguous() for x in (q_cpu, k_cpu, v_cpu, do_cpu))
+        doc_np = None if doc_np is None else np.ascontiguousarray(doc_np[bs])
+    Bl, Hl = q_cpu.shape[0], q_cpu.shape[1]
     bf = torch.bfloat16
     q = q_cpu.to(bf).to(dev).requires_grad_(True)
     k = k_cpu.to(bf).to(dev).requires_grad_(True)
     v = v_cpu.to(bf).to(dev).requires_grad_(True)
     do = do_cpu.to(bf).to(dev)
     doc = None if doc_np is None else torch.from_numpy(doc_np).to(dev)
-    scale = torch.full((1, H, 1, 1), scale_val, device=dev, requires_grad=True)
-    pairs = valid_pairs(args.workload, B, H, N, doc_np)
+    scale = torch.full((1, Hl, 1, 1), scale_val, device=dev, requires_grad=True)
+    pairs = valid_pairs(args.workload, Bl, Hl, N, doc_np)  # this rank's valid pairs
     flops_step = 14.0 * D * pairs
+    # FLOPs of the whole job per step: the one problem (split) or one problem per rank (weak)
+    flops_job = 14.0 * D * pairs_full * (1 if split else world)
 
     launches = {"fwd": 0, "bwd": 0}
 
@@ -422,21 +439,58 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    h2d = 4 * hq.numel() * hq.element_size()
-    d2h = 4 * hq.numel() * hq.element_size()
+    # whole-job bytes: each rank copies its own inputs in and its results out
+    h2d = world * 4 * hq.numel() * hq.element_size()
+    d2h = world * 4 * hq.numel() * hq.element_size()
 
     # a job takes as long as its slowest rank
     t_ms, e2e_ms, t_fwd, t_bwd = max_over_ranks([t_ms, e2e_ms, t_fwd, t_bwd], device=dev)
 
     peaks, peak_src = load_peaks()
-    value = world * flops_step * args.steps / (t_ms / 1e3) / 1e12
-    e2e_value = world * flops_step * e2e_steps / (e2e_ms / 1e3) / 1e12
+    value = flops_job * args.steps / (t_ms / 1e3) / 1e12
+    e2e_value = flops_job * e2e_steps / (e2e_ms / 1e3) / 1e12
+
+    # with the strong split, weak scaling as an extra figure: every rank runs a whole problem of
+    # its own (seeds offset by rank), same step, same timing rule
+    weak = None
+    if split:
+        wq, wk, wv, wdo, wdoc_np, _ = make_inputs(args.workload, rank)
+        wq, wk, wv = (x.to(bf).to(dev).requires_grad_(True) for x in (wq, wk, wv))
+        wdo = wdo.to(bf).to(dev)
+        wdoc = None if wdoc_np is None else torch.from_numpy(wdoc_np).to(dev)
+        wscale = torch.full((1, H, 1, 1), scale_val, device=dev, requires_grad=True)
+
+        def wstep():
+            o = flash_born_attention(wq, wk, wv, wscale, is_causal=causal, eps=1e-12, doc_ids=wdoc)
+            torch.autograd.grad(o, (wq, wk, wv, wscale), wdo)
+
+        for _ in range(args.warmup):
+            wstep()
+        wev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(min(args.steps, 200) * HEAD_START_CYCLES)
+        for i in range(args.steps):
+            flush.zero_()
+            wev[i][0].record()
+            wstep()
+            wev[i][1].record()
+        torch.cuda.synchronize()
+        (w_ms,) = max_over_ranks([sum(a.elapsed_time(b) for a, b in wev)], device=dev)
+        w_flops = torch.tensor([14.0 * D * valid_pairs(args.workload, B, H, N, wdoc_np)], dtype=torch.float64,
+                               device=dev)
+        dist.all_reduce(w_flops)  # every rank's problem counts (document masks differ per rank)
+        weak = {"value": float(w_flops.item()) * args.steps / (w_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": w_ms / args.steps, "scaling": "weak",
+                "what": f"every rank runs a whole {args.workload} problem of its own (global batch {B * world})"}
+        del wq, wk, wv, wdo
     flops_fwd = 4.0 * D * pairs
     flops_bwd = 10.0 * D * pairs
     dominant = "bwd" if t_bwd >= t_fwd else "fwd"
     dom_flops, dom_ms = (flops_bwd, t_bwd) if dominant == "bwd" else (flops_fwd, t_fwd)
     achieved = dom_flops / (dom_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic, traffic_src = profiled_traffic(args.workload, dominant)
 
     gpt = None if args.no_gpt else run_gpt(args, rank, world, dev)
 
@@ -457,23 +511,29 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "warmup": args.warmup,
             "ms_per_step": t_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": desc, "global_batch": B * world, "seq_len": N, "heads": H, "head_dim": D,
-                       "parallelism": f"batch x head split, {world} rank(s), no collective",
+            "config": {"workload": desc, "global_batch": B if split else B * world, "seq_len": N, "heads": H,
+                       "head_dim": D,
+                       "parallelism": (f"(batch, head) units split over {world} ranks, rank 0 holds batch "
+                                       f"[{shard.b0},{shard.b1}) x heads [{shard.h0},{shard.h1}) = {shard.units} "
+                                       "units; no collective" if split else
+                                       f"{world} rank(s), one whole problem each, no collective"),
                        "flops_per_step_per_rank": flops_step,
+                       "flops_per_step_job": flops_job,
                        "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush"},
+            "weak_scaling": weak,
             "per_gpu_tflops": value / world,
             "pct_of_bf16_peak_sustained": 100.0 * value / world / float(
                 peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])),
             "roofline": {"bound": "tensor", "kernel": f"{dominant} ({path_bwd if dominant == 'bwd' else path_fwd})",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                          "peak_source": f"bf16_tflops (burst) of {peak_src}",
-                         "traffic": profiled_traffic(args.workload, dominant),
-                         "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant "
-                                           "kernel, profiles/tc_*_kernel_c2.md (ncu capture of this build)",
+                         "traffic": traffic if world == 1 else None,
+                         "traffic_source": ("dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant "
+                                            "kernel, " + traffic_src) if world == 1 else "not profiled for a shard",
                          "fwd_ms": t_fwd, "bwd_ms": t_bwd, "fwd_launches": n_fwd_launch,
                          "bwd_launches": n_bwd_launch,
                          "fwd_tflops": flops_fwd / (t_fwd / 1e3) / 1e12,
@@ -760,6 +820,8 @@ def _path_is_tc(q: torch.Tensor, backward: bool) -> bool:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--weak", action="store_true",
+                    help="with N > 1: every rank runs a whole problem (weak scaling) instead of its shard of one")
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

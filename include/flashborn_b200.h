@@ -20,7 +20,8 @@
  *
  * Conventions
  *   - The caller owns every buffer (out, z, dq, dk, dv, dscale, dtau, workspace); the library
- *     never allocates or frees device memory.
+ *     never allocates or frees device memory.  One exception: fb_born_bwd_static_scratch's
+ *     fixed FB_STATIC_SCRATCH_BYTES array, part of the library's device module (see there).
  *   - Tensors are (B, H, T, D) with arbitrary element strides (the innermost stride must be 1 for
  *     the tensor-core path; other layouts run on the general path). doc_ids is (B, T) int32.
  *   - scale / tau are device fp32 vectors of 1 (shared) or H (per head) elements.
@@ -228,13 +229,18 @@ FB_API int fb_heads_epilogue_fwd(const fb_heads_args* args, void* stream);
 FB_API int fb_heads_epilogue_bwd(const fb_heads_args* args, void* stream);
 
 /* Plain flash-Born backward that allocates nothing and takes no workspace: its scratch is a
- * fixed FB_STATIC_SCRATCH_BYTES device array inside the library (one per GPU, held from the
- * first call on that GPU until exit).  For callers that cannot allocate device memory (a host
- * runtime with no device allocator of its own, or a step that must not call cudaMalloc).
+ * fixed FB_STATIC_SCRATCH_BYTES device array inside the library, for callers that cannot
+ * allocate device memory (a host runtime with no device allocator of its own, or a step that
+ * must not call cudaMalloc).  The array belongs to the library's device module: every GPU holds
+ * it from the time the module loads there until exit (with CUDA's default lazy module loading,
+ * the first launch of any of this library's kernels on that GPU; with CUDA_MODULE_LOADING=EAGER,
+ * context creation), whether or not this entry point is called.
  * Same arguments and results as fb_born_bwd except workspace/workspace_bytes, which it ignores.
- * Returns FB_ERR_SCRATCH_LIMIT when fb_bwd_workspace_size() exceeds FB_STATIC_SCRATCH_BYTES.
- * The first call on a device looks up the array's address there; make it before any stream
- * capture.  All calls on a device share the array: calls that overlap on the GPU race.
+ * Returns FB_ERR_SCRATCH_LIMIT when fb_bwd_workspace_size() exceeds FB_STATIC_SCRATCH_BYTES, and
+ * FB_ERR_ARG for purified arguments (tau != NULL): plain Born only.
+ * The first successful call on a device looks up the array's address there; make it before any
+ * stream capture.  All calls on a device share the array, which keeps the last call's contents
+ * (each call rewrites what it reads): calls that overlap on the GPU race.
  * No counterpart in the reference (its kernels allocate through PyTorch). */
 #define FB_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
 FB_API int fb_born_bwd_static_scratch(const fb_attn_args* args, void* stream);

@@ -88,6 +88,15 @@ def _chunks(T: int, chunk: int):
         yield m0, min(T, m0 + chunk)
 
 
+def _key_span(m0: int, m1: int, T: int, is_causal: bool, window_size: int) -> tuple[int, int]:
+    """Keys ``[lo, hi)`` that can pair with queries ``[m0, m1)``: causal stops at ``m1``; a window
+    starts at ``m0 - window + 1`` (``diff < window``, ``flash_born.py:635-652``).  Pairs outside the
+    span are masked anyway, so restricting the columns to it changes no result, only the cost."""
+    lo = max(0, m0 - int(window_size) + 1) if window_size > 0 else 0
+    hi = m1 if is_causal else T
+    return lo, max(lo, hi)
+
+
 def count_valid_pairs(T: int, is_causal: bool, window_size: int, doc_ids_row: np.ndarray | None) -> int:
     """Number of (i, j) pairs with valid(i, j) for one (batch, head) -- the FLOP-count unit."""
     if doc_ids_row is None:
@@ -126,19 +135,20 @@ def born_forward(q, k, v, scale, is_causal=True, eps=1e-12, window_size=0, doc_i
     sc = _per_head(scale, H, dt)
     out = np.zeros_like(v)
     z = np.zeros((B, H, T), dtype=dt)
-    cols = np.arange(T)
     for b in range(B):
         for h in range(H):
             for m0, m1 in _chunks(T, chunk):
                 rows = np.arange(m0, m1)
+                c0, c1 = _key_span(m0, m1, T, is_causal, window_size)
+                cols = np.arange(c0, c1)
                 mask = valid_mask(rows, cols, is_causal, window_size,
                                   None if doc_ids is None else doc_ids[b, m0:m1],
-                                  None if doc_ids is None else doc_ids[b])
-                raw = q[b, h, m0:m1] @ k[b, h].T
+                                  None if doc_ids is None else doc_ids[b, c0:c1])
+                raw = q[b, h, m0:m1] @ k[b, h, c0:c1].T
                 a = np.where(mask, np.maximum(raw * sc[h], 0), 0).astype(dt)
                 p = a * a
                 zz = p.sum(axis=1) + dt.type(eps)
-                out[b, h, m0:m1] = (p @ v[b, h]) / zz[:, None]
+                out[b, h, m0:m1] = (p @ v[b, h, c0:c1]) / zz[:, None]
                 z[b, h, m0:m1] = zz
     return out, z
 
@@ -167,26 +177,27 @@ def born_backward(q, k, v, out, z, dout, scale, is_causal=True, window_size=0, d
     dk = np.zeros_like(k)
     dv = np.zeros_like(v)
     dscale = np.zeros((H,), dtype=dt)
-    cols = np.arange(T)
     for b in range(B):
         for h in range(H):
             for m0, m1 in _chunks(T, chunk):
                 rows = np.arange(m0, m1)
+                c0, c1 = _key_span(m0, m1, T, is_causal, window_size)
+                cols = np.arange(c0, c1)
                 mask = valid_mask(rows, cols, is_causal, window_size,
                                   None if doc_ids is None else doc_ids[b, m0:m1],
-                                  None if doc_ids is None else doc_ids[b])
-                raw = q[b, h, m0:m1] @ k[b, h].T
+                                  None if doc_ids is None else doc_ids[b, c0:c1])
+                raw = q[b, h, m0:m1] @ k[b, h, c0:c1].T
                 a = np.where(mask, np.maximum(raw * sc[h], 0), 0).astype(dt)
                 zz = z[b, h, m0:m1][:, None]
                 w = (a * a) / zz
                 do = dout[b, h, m0:m1]
-                dv[b, h] += w.T @ do
+                dv[b, h, c0:c1] += w.T @ do
                 delta = np.sum(do * out[b, h, m0:m1], axis=1)[:, None]
-                dp = (do @ v[b, h].T - delta) / zz
+                dp = (do @ v[b, h, c0:c1].T - delta) / zz
                 ds = np.where(mask, 2 * a * dp, 0).astype(dt)
                 dscale[h] += np.sum(ds * raw)
-                dk[b, h] += (ds.T @ q[b, h, m0:m1]) * sc[h]
-                dq[b, h, m0:m1] = (ds @ k[b, h]) * sc[h]
+                dk[b, h, c0:c1] += (ds.T @ q[b, h, m0:m1]) * sc[h]
+                dq[b, h, m0:m1] = (ds @ k[b, h, c0:c1]) * sc[h]
     return BornGrads(dq, dk, dv, dscale)
 
 
@@ -209,20 +220,21 @@ def purified_forward(q, k, v, gamma, tau, eps_base=0.05, is_causal=True, eps=1e-
     t = _per_head(tau, H, dt)
     out = np.zeros_like(v)
     z = np.zeros((B, H, T), dtype=dt)
-    cols = np.arange(T)
     for b in range(B):
         for h in range(H):
             for m0, m1 in _chunks(T, chunk):
                 rows = np.arange(m0, m1)
+                c0, c1 = _key_span(m0, m1, T, is_causal, window_size)
+                cols = np.arange(c0, c1)
                 mask = valid_mask(rows, cols, is_causal, window_size,
                                   None if doc_ids is None else doc_ids[b, m0:m1],
-                                  None if doc_ids is None else doc_ids[b])
-                raw = q[b, h, m0:m1] @ k[b, h].T
+                                  None if doc_ids is None else doc_ids[b, c0:c1])
+                raw = q[b, h, m0:m1] @ k[b, h, c0:c1].T
                 u = np.where(mask, np.maximum(g[h] * (raw - t[h]), 0), 0).astype(dt)
                 bb = np.where(mask, np.maximum(raw, 0), 0).astype(dt)
                 p = (u * u) * (u * u) + dt.type(eps_base) * (bb * bb)
                 zz = p.sum(axis=1) + dt.type(eps)
-                out[b, h, m0:m1] = (p @ v[b, h]) / zz[:, None]
+                out[b, h, m0:m1] = (p @ v[b, h, c0:c1]) / zz[:, None]
                 z[b, h, m0:m1] = zz
     return out, z
 
@@ -246,27 +258,28 @@ def purified_backward(q, k, v, out, z, dout, gamma, tau, eps_base=0.05, is_causa
     dv = np.zeros_like(v)
     dgamma = np.zeros((H,), dtype=dt)
     dtau = np.zeros((H,), dtype=dt)
-    cols = np.arange(T)
     for b in range(B):
         for h in range(H):
             for m0, m1 in _chunks(T, chunk):
                 rows = np.arange(m0, m1)
+                c0, c1 = _key_span(m0, m1, T, is_causal, window_size)
+                cols = np.arange(c0, c1)
                 mask = valid_mask(rows, cols, is_causal, window_size,
                                   None if doc_ids is None else doc_ids[b, m0:m1],
-                                  None if doc_ids is None else doc_ids[b])
-                raw = q[b, h, m0:m1] @ k[b, h].T
+                                  None if doc_ids is None else doc_ids[b, c0:c1])
+                raw = q[b, h, m0:m1] @ k[b, h, c0:c1].T
                 u = np.where(mask, np.maximum(g[h] * (raw - t[h]), 0), 0).astype(dt)
                 bb = np.where(mask, np.maximum(raw, 0), 0).astype(dt)
                 p = (u * u) * (u * u) + eb * (bb * bb)
                 zz = z[b, h, m0:m1][:, None]
                 do = dout[b, h, m0:m1]
-                dv[b, h] += (p / zz).T @ do
+                dv[b, h, c0:c1] += (p / zz).T @ do
                 delta = np.sum(do * out[b, h, m0:m1], axis=1)[:, None]
-                dp = (do @ v[b, h].T - delta) / zz
+                dp = (do @ v[b, h, c0:c1].T - delta) / zz
                 du = 4 * (u * u * u) * dp
                 draw = np.where(mask, du * g[h] + 2 * eb * bb * dp, 0).astype(dt)
                 dgamma[h] += np.sum(du * (raw - t[h]))
                 dtau[h] += np.sum(-du * g[h])
-                dk[b, h] += draw.T @ q[b, h, m0:m1]
-                dq[b, h, m0:m1] = draw @ k[b, h]
+                dk[b, h, c0:c1] += draw.T @ q[b, h, m0:m1]
+                dq[b, h, m0:m1] = draw @ k[b, h, c0:c1]
     return BornGrads(dq, dk, dv, dgamma, dtau)

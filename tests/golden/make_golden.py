@@ -179,6 +179,51 @@ def main(src: str) -> None:
         params=dict(scale=np.array(1.0, dtype=np.float32), is_causal=True, eps=1e-12, window_size=0, doc_ids=None),
         grad=("scale",))
 
+    # eps large enough that the parameter gradients are far from zero, so the closed forms of the
+    # B200 backward (dscale = (2 / scale) sum eps delta / Z, dgamma = (4 / gamma)(sum eps delta / Z
+    # - sum eps_base b^2 dP)) are gated relative to their own size.  The first mirrors the shape,
+    # seed, eps 1e-6 and per-head (H,) scale of the reference's JAX parity test
+    # (tests/test_jax_haliax.py:74-135, torch side).
+    rng = np.random.default_rng(123)
+    B, H, T, D = 2, 2, 16, 8
+    q, k, v, do = (rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(4))
+    cases["plain_eps1e-6_perhead_d8"] = dict(
+        kind="plain", q=q, k=k, v=v, do=do,
+        params=dict(scale=np.array([2.5, 3.2], dtype=np.float32), is_causal=True, eps=1e-6, window_size=0,
+                    doc_ids=None),
+        grad=("scale",))
+    rng = np.random.default_rng(1)
+    B, H, T, D = 1, 3, 200, 64
+    q = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    k = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    v, do = (rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(2))
+    cases["plain_eps1e-2_perhead_d64"] = dict(
+        kind="plain", q=q, k=k, v=v, do=do,
+        params=dict(scale=np.array([2.0, 4.0, 8.0], dtype=np.float32).reshape(1, H, 1, 1), is_causal=True,
+                    eps=1e-2, window_size=0, doc_ids=None),
+        grad=("scale",))
+    rng = np.random.default_rng(3)
+    B, H, T, D = 2, 2, 150, 64
+    q = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    k = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    v, do = (rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(2))
+    cases["plain_eps0.5_window_shared_d64"] = dict(
+        kind="plain", q=q, k=k, v=v, do=do,
+        params=dict(scale=np.array(3.0, dtype=np.float32), is_causal=False, eps=0.5, window_size=40,
+                    doc_ids=None),
+        grad=("scale",))
+    rng = np.random.default_rng(2)
+    B, H, T, D = 1, 3, 200, 64
+    q = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    k = _l2n(rng.standard_normal((B, H, T, D))).astype(np.float32)
+    v, do = (rng.standard_normal((B, H, T, D)).astype(np.float32) for _ in range(2))
+    cases["purified_eps0.3_perhead_d64"] = dict(
+        kind="purified", q=q, k=k, v=v, do=do,
+        params=dict(scale=np.array([4.0, 8.0, 11.0], dtype=np.float32),
+                    tau=np.array([0.02, 0.05, 0.08], dtype=np.float32),
+                    eps_base=0.05, is_causal=True, eps=0.3, window_size=0, doc_ids=None),
+        grad=("scale", "tau"))
+
     manifest = {}
     for name, c in cases.items():
         fn = fb if c["kind"] == "plain" else fpb
