@@ -335,6 +335,48 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Packed fp32 pairs: sm_100 executes add / mul / fma on two fp32 lanes of a 64-bit register pair
+// in one instruction (PTX .f32x2, round-to-nearest like the scalar forms, so results are
+// bitwise those of two scalar operations).  Adjacent TMEM columns land in adjacent registers,
+// which is the pairing these take.
+// ---------------------------------------------------------------------------------------------
+struct f32x2 {
+  uint64_t r;
+};
+__device__ __forceinline__ f32x2 f2_make(float lo, float hi) {
+  f32x2 v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v.r) : "f"(lo), "f"(hi));
+  return v;
+}
+__device__ __forceinline__ float f2_lo(f32x2 v) { return __uint_as_float(static_cast<uint32_t>(v.r)); }
+__device__ __forceinline__ float f2_hi(f32x2 v) { return __uint_as_float(static_cast<uint32_t>(v.r >> 32)); }
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d.r) : "l"(a.r), "l"(b.r));
+  return d;
+}
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d.r) : "l"(a.r), "l"(b.r), "l"(c.r));
+  return d;
+}
+// The pair rounded to bf16 and packed (low half = lo), one cvt instruction.
+__device__ __forceinline__ uint32_t f2_bf16(f32x2 v) {
+  uint32_t d;
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v.r));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// max(0, lo), max(0, hi) rounded to bf16 and packed (low half = lo), one cvt instruction.
+__device__ __forceinline__ uint32_t relu_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 // The two halves of a packed bf16 pair as floats.
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }

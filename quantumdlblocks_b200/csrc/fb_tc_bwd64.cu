@@ -8,7 +8,7 @@
 //
 // Four launches (all on the caller's stream; two more compute the document spans when document
 // ids are given):
-//   1. bwd_prep_kernel   delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
+//   1. bwd_prep_kernel   -delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
 //                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
 //   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
 //                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
@@ -93,7 +93,7 @@ struct BwdParams {
   int64_t dk_s0, dk_s1, dk_s2;
   __nv_bfloat16* dv;
   int64_t dv_s0, dv_s1, dv_s2;
-  const float* dlz;    // [BH][Tpad]  delta_i / Z_i
+  const float* dlz;    // [BH][Tpad]  -delta_i / Z_i
   const float* zinv;   // [BH][Tpad]  1 / Z_i
   float* dq_acc;       // [BH][Tpad][64]
   float* partials;     // [BH][n_kv][8 warps][2]
@@ -527,22 +527,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t wpk[8], gpk[8];
 #pragma unroll
           for (int e = 0; e < 16; e += 2) {
-            float wv[2], gv[2];
+            if constexpr (kFold) {
+              // vectors carry scale^2 (dc = -scale^2 delta / Z): W = b (b scale^2 / Z),
+              // G / 2 = b (dP^T scale^2 / Z - scale^2 delta / Z); two query columns per packed op
+              const f32x2 b = f2_make(fmaxf(__uint_as_float(rs[e]), 0.f), fmaxf(__uint_as_float(rs[e + 1]), 0.f));
+              const f32x2 z = f2_make(zc[e], zc[e + 1]);
+              const f32x2 r = f2_make(__uint_as_float(rd[e]), __uint_as_float(rd[e + 1]));
+              wpk[e / 2] = f2_bf16(f2_mul(f2_mul(b, z), b));
+              gpk[e / 2] = f2_bf16(f2_mul(b, f2_fma(r, z, f2_make(dc[e], dc[e + 1]))));
+            } else {
+              float wv[2], gv[2];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const float raw = __uint_as_float(rs[e + u]);
-              if constexpr (kFold) {
-                // vectors carry scale^2: W = b (b scale^2 / Z), G / 2 = b (dP^T scale^2 / Z - scale^2 delta / Z)
-                const float b = fmaxf(raw, 0.f);
-                wv[u] = (b * zc[e + u]) * b;
-                gv[u] = b * fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]);
-              } else {
+              for (int u = 0; u < 2; ++u) {
+                const float raw = __uint_as_float(rs[e + u]);
                 wv[u] = map.prob(raw, true) * zc[e + u];
-                gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], -dc[e + u]), g1, g2);
+                gv[u] = map.grad(raw, true, fmaf(__uint_as_float(rd[e + u]), zc[e + u], dc[e + u]), g1, g2);
               }
+              wpk[e / 2] = pack2<true>(wv[0], wv[1]);
+              gpk[e / 2] = pack2<true>(gv[0], gv[1]);
             }
-            wpk[e / 2] = pack2<true>(wv[0], wv[1]);
-            gpk[e / 2] = pack2<true>(gv[0], gv[1]);
           }
           tmem_st8(s_col + sc * 8, wpk);
           tmem_st8(p_col + sc * 8, gpk);
@@ -722,7 +725,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
       // plain map: the main kernel expects both vectors times scale^2
       const float sc = a.scale[a.scale_per_head ? h : 0];
       const float f = a.purified ? 1.f : sc * sc;
-      a.dlz[row] = (s * zi) * f;
+      a.dlz[row] = -((s * zi) * f);  // negated: the main kernel adds it in one fused multiply-add
       a.zinv[row] = zi * f;
       csum += a.eps * s * zi;
     }

@@ -44,6 +44,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "fb_common.cuh"
 #include "fb_sm100.cuh"
@@ -399,11 +400,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           // four 32-column chunks, software pipelined: the TMEM load of chunk c+1 is in flight
           // while chunk c is turned into P (the loads would otherwise expose their latency)
           uint32_t ra[32], rb[32];
+          f32x2 sc2{};
+          if constexpr (std::is_same<Map, PlainMap>::value) sc2 = f2_make(map.scale, map.scale);
           auto chunk = [&](int c, const uint32_t (&r)[32]) {
             uint32_t w[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), true), map.prob(__uint_as_float(r[e + 1]), true));
+              if constexpr (std::is_same<Map, PlainMap>::value) {
+                // p = relu(x)^2 = relu(x |x|) with x = scale raw: one packed multiply for the
+                // pair, one multiply each (|x| is an operand modifier) and the ReLU in the cvt
+                const f32x2 x = f2_mul(f2_make(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2);
+                const float x0 = f2_lo(x), x1 = f2_hi(x);
+                w[e / 2] = relu_bf16x2(x0 * fabsf(x0), x1 * fabsf(x1));
+              } else {
+                w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), true), map.prob(__uint_as_float(r[e + 1]), true));
+              }
               if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
             }
             tmem_st16(p_addr + c * 16, w);
