@@ -5,7 +5,8 @@
 // walks the key tiles (128 keys) that can hold valid pairs (causal / window tile skipping, as
 // flash_born.py:152-156).  The tile sequence is flattened across items, so the TMA ring, the
 // TMEM double buffers and the mbarrier phases run on from one item into the next and the
-// per-item set-up latency is hidden.  Warp-specialised pipeline (352 threads):
+// per-item set-up latency is hidden.  Warp-specialised pipeline (480 threads for d=64, 352 for
+// d=128, which has no epilogue warpgroup):
 //
 //   warp 0      TMA producers: copies issued by one thread complete one after another (about
 //               0.3 us each, whatever their size), so lane 0 requests Q of an item (double-
@@ -30,8 +31,14 @@
 //               (TMEM buffers S[w], P[w]); thread r of a group owns TMEM lane r = query row r.
 //               tcgen05.ld S row -> a = relu(scale s) (masked), p = a^2, P = bf16(p) ->
 //               tcgen05.st into P[w], Z += the bf16-rounded p.  No exp, no running max, no
-//               rescale of O: per item the groups add their row sums, read O once, multiply by
-//               1 / Z (Z = sum p + eps) and store O (each group half the columns) and Z.
+//               rescale of O.  d=64: at an item's end the groups go straight on to the next
+//               item.  d=128: the groups add their row sums, read O once, multiply by 1 / Z and
+//               store O (each group half the columns) and Z.
+//   warps 11-14 (d=64) epilogue warpgroup: per item, once the last O += P V has landed, read O (and Z)
+//               from TMEM, release O to the next item's first product, store O * (1 / Z) and Z
+//               (Z = sum p + eps).  The pointwise groups never wait at item boundaries: in
+//               traces of the earlier layout, where they ran the epilogue themselves, about a
+//               third of a CTA's time went to waiting for the item's last product and the store.
 //
 // Numerics: S and O accumulate in fp32 and PV consumes p rounded to bf16, as in the reference
 // kernel (flash_born.py:156-191).  Z sums the same bf16-rounded p that PV consumes (the reference
@@ -56,11 +63,15 @@ using namespace sm100;
 
 constexpr int kBM = 128;       // queries per item (one M=128 MMA)
 constexpr int kBN = 128;       // keys per tile
-constexpr int kThreads = 352;  // 11 warps
+constexpr int kMaxThreads = 480;  // 15 warps (d = 64), 11 warps (d = 128)
 constexpr uint32_t kTmemCols = 512;
 
 template <int D>
 struct FwdCfg {
+  // d=64 runs the item epilogue in a warpgroup of its own (warps 11-14); d=128 keeps it in the
+  // pointwise groups: its pointwise body wants ~170 registers, more than 480 threads can have
+  static constexpr bool kEpiWarps = D == 64;
+  static constexpr int kThreads = kEpiWarps ? 480 : 352;
   static constexpr int kStages = D == 64 ? 5 : 2;
   // d=64: Z comes from the tensor core (the PV product is widened to N = 80 with a ones block
   // as the extra B columns, into the 16 TMEM columns after O); d=128 has no spare columns and
@@ -139,7 +150,7 @@ __device__ __forceinline__ Item item_at(const FwdParams& p, int idx) {
 }
 
 template <int D, class Map, bool kHasDoc, typename TO>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
   using Cfg = FwdCfg<D>;
@@ -158,8 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pv_done = bars + 8 + 4 * S;  // [2]
   uint64_t* o_full = bars + 10 + 4 * S;
   uint64_t* o_empty = bars + 11 + 4 * S;
-  uint64_t* z_bar = bars + 12 + 4 * S;
-  uint64_t* drain = bars + 13 + 4 * S;
+  uint64_t* z_bar = bars + 12 + 4 * S;   // the groups' row sums (d = 128)
+  uint64_t* drain = bars + 13 + 4 * S;   // [2]
   static_assert(15 + 4 * S <= 48, "barrier area");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 48);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 49);
@@ -185,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_empty[st], 1);
     }
     mbar_init(o_full, 1);
-    mbar_init(o_empty, 256);
+    mbar_init(o_empty, Cfg::kEpiWarps ? 128 : 256);  // the epilogue warpgroup, or both pointwise groups
     mbar_init(z_bar, 256);
     mbar_init(drain, 1);
     mbar_init(drain + 1, 1);
@@ -194,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if constexpr (Cfg::kTcZ) {  // the ones tile read by the Z product (B operand)
     uint32_t* ones = reinterpret_cast<uint32_t*>(smem + Cfg::kOnesOff);
-    for (int x = threadIdx.x; x < 2048 / 4; x += kThreads) ones[x] = 0x3F803F80u;  // bf16 1.0 pairs
+    for (int x = threadIdx.x; x < 2048 / 4; x += Cfg::kThreads) ones[x] = 0x3F803F80u;  // bf16 1.0 pairs
     fence_proxy_async_smem();
   }
   if (warp == 0 && lane == 0) {
@@ -335,6 +346,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
+  } else if (Cfg::kEpiWarps && warp >= 11) {
+    // ------------------------------------------------------------------ epilogue warpgroup (warps 11-14)
+    // Per item: wait until the last O += P V has landed, read O and Z from TMEM, release O to the next item's first product, and store
+    // O * (1 / Z) and Z.  Thread r of the group owns TMEM lane r = query row r (warp 11 + x
+    // reads lane quadrant (11 + x) % 4).
+    const int lg = warp & 3;
+    const int row = lg * 32 + lane;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
+    bool ok = true;
+    int i = 0;
+    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      const Item it = item_at(p, idx);
+      const int qi = it.m0 + row;
+      static_assert(!Cfg::kEpiWarps || Cfg::kTcZ, "the epilogue warpgroup reads Z from TMEM");
+      ok = __all_sync(0xffffffffu, mbar_wait(o_full, i & 1, wc, 11));
+      if (!ok) break;
+      tc_fence_after();
+      const float zden = __uint_as_float(tmem_ld1(lane_addr + Cfg::kTmemZ)) + p.eps;
+      const float inv = 1.f / zden;
+      TO* orow = reinterpret_cast<TO*>(p.out) + (int64_t)it.b * p.o_s0 + (int64_t)it.h * p.o_s1 + (int64_t)qi * p.o_s2;
+      // 64 columns per round (d = 128: two rounds), O released after the last round's loads
+#pragma unroll
+      for (int hf = 0; hf < D / 64; ++hf) {
+        uint32_t r[64];
+        tmem_ld32(lane_addr + Cfg::kTmemO + hf * 64, *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(lane_addr + Cfg::kTmemO + hf * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        tmem_wait_ld();
+        if (hf == D / 64 - 1) {
+          tc_fence_before();
+          mbar_arrive(o_empty);
+        }
+        if (qi < p.T) {
+          if constexpr (sizeof(TO) == 2) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + hf * 64);
+#pragma unroll
+            for (int v4 = 0; v4 < 8; ++v4)
+              dst[v4] = make_uint4(pack2<true>(__uint_as_float(r[8 * v4]) * inv, __uint_as_float(r[8 * v4 + 1]) * inv),
+                                   pack2<true>(__uint_as_float(r[8 * v4 + 2]) * inv, __uint_as_float(r[8 * v4 + 3]) * inv),
+                                   pack2<true>(__uint_as_float(r[8 * v4 + 4]) * inv, __uint_as_float(r[8 * v4 + 5]) * inv),
+                                   pack2<true>(__uint_as_float(r[8 * v4 + 6]) * inv, __uint_as_float(r[8 * v4 + 7]) * inv));
+          } else {
+            float4* dst = reinterpret_cast<float4*>(orow + hf * 64);
+#pragma unroll
+            for (int v4 = 0; v4 < 16; ++v4)
+              dst[v4] = make_float4(__uint_as_float(r[4 * v4]) * inv, __uint_as_float(r[4 * v4 + 1]) * inv,
+                                    __uint_as_float(r[4 * v4 + 2]) * inv, __uint_as_float(r[4 * v4 + 3]) * inv);
+          }
+        }
+      }
+      if (qi < p.T) p.z[((int64_t)it.b * p.H + it.h) * p.T + qi] = zden;
+    }
   } else {
     // ------------------------------------------------------------------ pointwise warpgroups (warps 2-9)
     const int wg = (warp - 2) >> 2;
@@ -483,7 +545,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&p_full[wg]);
       }
       if (idx + (int)gridDim.x < p.n_items) fetch(idx + gridDim.x);
-      // ---- epilogue of the item: Z (tensor-core sum, or the two groups' row sums), O * (1 / Z)
+      if constexpr (Cfg::kEpiWarps) {  // the epilogue warpgroup takes the item's O; go straight on
+        g += it.n_count;
+        continue;
+      }
+      // ---- epilogue of the item (d = 128): Z (the two groups' row sums), O * (1 / Z)
       float* zp = zpart + (i & 1) * 2 * kBM;
       if constexpr (!Cfg::kTcZ) {
         zp[wg * kBM + row] = zsum;
@@ -562,7 +628,7 @@ int launch_fwd(const Problem& pr, cudaStream_t s, const FwdParams& fp, const CUt
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   dim3 grid(std::min(fp.n_items, num_sms()));
-  kernel<<<grid, kThreads, smem, s>>>(mq, mk, mv, fp);
+  kernel<<<grid, FwdCfg<D>::kThreads, smem, s>>>(mq, mk, mv, fp);
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   return FB_OK;
