@@ -6,10 +6,12 @@
 // runs; callers that ask for deterministic gradients get the two-kernel backward of fb_tc_bwd.cu,
 // which also serves head dim 128 (whose accumulators do not fit in TMEM next to dQ's).
 //
-// Four launches (all on the caller's stream; two more compute the document spans when document
-// ids are given):
+// Three launches for the plain map, four for the purified one (all on the caller's stream; two
+// more compute the document spans when document ids are given):
 //   1. bwd_prep_kernel   -delta_i / Z_i with delta_i = sum_d dO_id O_id, 1/Z_i (per-head rows padded
-//                        to a multiple of 64), and a zeroed fp32 dQ accumulator (workspace)
+//                        to a multiple of 64), a zeroed fp32 dQ accumulator (workspace), and for the
+//                        plain map the closed-form dscale, added per 64-row chunk (float atomics:
+//                        this backward is the non-deterministic one)
 //   2. tc_bwd_kernel     persistent: one CTA per SM walks work items (batch, head, 128-key tile)
 //                        in L2-resident windows of heads (bwd_next); each item walks the 64-query
 //                        tiles that can hold valid pairs and accumulates dK, dV in TMEM; dQ
@@ -17,8 +19,8 @@
 //                        reduce-add.  The query-tile pipeline runs on across items (K, V
 //                        double-buffered per item)
 //   3. bwd_post_kernel   dQ = accumulator -> input dtype
-//   4. bwd_param_kernel  fixed-order sums into dscale / dtau from the pre-pass's closed-form
-//                        sums and the main kernel's per-CTA partials
+//   4. bwd_param_kernel  purified only: fixed-order sums into d gamma / d tau from the pre-pass's
+//                        closed-form sums and the main kernel's per-CTA partials
 //
 // Per (key tile, query tile) the main kernel runs the five products the algorithm needs
 // (the reference's two kernels run six, flash_born.py:267-312 and :398-427):
@@ -742,6 +744,13 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const AuxParams a) {
     float t = 0.f;
     for (int w = 0; w < 8; ++w) t += csum_w[w];
     a.prep_part[bh * (a.Tpad / 64) + chunk] = t;
+    // plain map: dscale_h = (2 / scale_h) sum_{b,i} eps delta_i / Z_i is complete here; this
+    // (non-deterministic) backward adds each chunk's share directly, in whatever order the blocks
+    // run, as the reference's per-head atomic does (flash_born.py:319-322)
+    if (!a.purified && a.dscale != nullptr) {
+      const float sc = a.scale[a.scale_per_head ? h : 0];
+      atomicAdd(&a.dscale[a.scale_per_head ? h : 0], (2.f / sc) * t);
+    }
   }
 }
 
@@ -979,13 +988,15 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   bwd_post_kernel<<<(unsigned)((post_threads + 255) / 256), 256, 0, s>>>(a);
   float* head_terms = reinterpret_cast<float*>(ws + w.head_terms);
   int n = 3 + (pr.doc != nullptr ? 2 : 0);
-  if (!pr.given_norm) {  // a term of a sum leaves the parameter gradients to its caller
+  // plain map: the pre-pass has added dscale already; purified: d gamma and d tau also need the
+  // main kernel's partials, summed in a fixed order here
+  if (!pr.given_norm && pr.purified) {  // a term of a sum leaves the parameter gradients to its caller
     bwd_param_kernel<<<pr.H, 256, 0, s>>>(a, head_terms);
     ++n;
-  }
-  if (!pr.given_norm && (!pr.scale_per_head || (pr.purified && !pr.tau_per_head))) {
-    bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
-    ++n;
+    if (!pr.scale_per_head || !pr.tau_per_head) {
+      bwd_param_shared_kernel<<<1, 1, 0, s>>>(a, head_terms);
+      ++n;
+    }
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
