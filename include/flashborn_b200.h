@@ -245,6 +245,17 @@ FB_API int fb_heads_epilogue_bwd(const fb_heads_args* args, void* stream);
 #define FB_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
 FB_API int fb_born_bwd_static_scratch(const fb_attn_args* args, void* stream);
 
+/* Test hook, not for production use: the plain forward on the tensor-core path (FB_ERR_UNSUPPORTED
+ * where that path does not apply) with every device-side wait bounded by wait_limit_us
+ * microseconds instead of one second, and CTA 0's producer never requesting its first K tile.
+ * The waits on that tile run into their bound, so the CTA takes the path a broken pipeline would:
+ * it raises its abort flag, lets the copies and products already in flight land (each wait again
+ * bounded), frees its tensor memory and returns, and the device status word reads FB_ERR_TIMEOUT
+ * with the site of the first wait that gave up (fb_device_status).  Nothing faults, traps or
+ * hangs; the context stays usable; this call's out and z are invalid.
+ * No counterpart in the reference. */
+FB_API int fb_test_born_fwd_timeout(const fb_attn_args* args, void* stream, uint32_t wait_limit_us);
+
 /* Bytes of device workspace the backward needs for these arguments (0 allowed for none).
  * A non-NULL tau marks purified arguments here and in fb_select_path.
  * The reference allocates the equivalent scratch implicitly (delta is recomputed per tile). */

@@ -134,6 +134,7 @@ SIGNATURES = {
     "fb_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_born_bwd_static_scratch": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_born_bwd_term": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
+    "fb_test_born_fwd_timeout": (ctypes.c_int, [_PARGS, ctypes.c_void_p, ctypes.c_uint32]),
     "fb_purified_born_fwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_purified_born_bwd": (ctypes.c_int, [_PARGS, ctypes.c_void_p]),
     "fb_bwd_workspace_size": (ctypes.c_size_t, [_PARGS]),

@@ -134,7 +134,14 @@ size_t workspace_for(const Problem& p, int path, bool backward) {
   return use_fused_bwd(p) ? tc_bwd64_workspace(p) : tc_bwd_workspace(p);
 }
 
-int run(const fb_attn_args* a, void* stream, bool purified, bool backward, bool given_norm = false) {
+// Test hook of fb_test_born_fwd_timeout: a short bound on every device-side wait and a forward
+// whose CTA 0 never requests its first K tile.
+struct TestHook {
+  uint64_t wait_limit_ns;
+};
+
+int run(const fb_attn_args* a, void* stream, bool purified, bool backward, bool given_norm = false,
+        const TestHook* hook = nullptr) {
   Problem p;
   int rc = normalise(a, purified, backward, &p, false, given_norm);
   if (rc != FB_OK) return rc;
@@ -146,6 +153,11 @@ int run(const fb_attn_args* a, void* stream, bool purified, bool backward, bool 
   }
   const int path = choose_path(a, p, backward);
   if (path < 0) return -path;
+  if (hook != nullptr) {
+    if (backward || path != FB_PATH_TCGEN05) return FB_ERR_UNSUPPORTED;
+    p.wait_limit_ns = hook->wait_limit_ns;
+    p.test_skip_first_k = 1;
+  }
   const size_t ws_need = workspace_for(p, path, backward);
   if (p.ws_bytes < ws_need || (p.ws == nullptr && ws_need > 0)) return FB_ERR_WORKSPACE;
   p.status = status_ptr(&rc);
@@ -182,6 +194,12 @@ int fb_born_bwd(const fb_attn_args* args, void* stream) { return fb::run(args, s
 int fb_purified_born_fwd(const fb_attn_args* args, void* stream) { return fb::run(args, stream, true, false); }
 int fb_purified_born_bwd(const fb_attn_args* args, void* stream) { return fb::run(args, stream, true, true); }
 int fb_born_bwd_term(const fb_attn_args* args, void* stream) { return fb::run(args, stream, false, true, true); }
+
+int fb_test_born_fwd_timeout(const fb_attn_args* args, void* stream, uint32_t wait_limit_us) {
+  if (wait_limit_us == 0) return FB_ERR_ARG;
+  const fb::TestHook hook{static_cast<uint64_t>(wait_limit_us) * 1000ull};
+  return fb::run(args, stream, false, false, false, &hook);
+}
 
 size_t fb_bwd_workspace_size(const fb_attn_args* args) {
   fb::Problem p;

@@ -46,6 +46,10 @@ struct Problem {
   void* ws;
   size_t ws_bytes;
   int* status;  // device status word [2]: {code, site}
+  // test hook (fb_test_born_fwd_timeout): bound of every device-side wait (0: the default) and
+  // whether CTA 0 of the tensor-core forward skips its first K-tile copy
+  uint64_t wait_limit_ns;
+  int test_skip_first_k;
 };
 
 // Device status codes written into Problem::status.

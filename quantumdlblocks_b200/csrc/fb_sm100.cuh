@@ -79,6 +79,7 @@ constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 struct WaitCtx {
   volatile int* abort_flag;  // shared memory
   int* status;               // global device status word {code, site}
+  uint64_t limit_ns = kWaitLimitNs;
 };
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& w, int site) {
@@ -89,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if (mbar_try_wait(bar, parity)) return true;
     if ((++it & 15u) == 0) {
       if (*w.abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > w.limit_ns) {
         *w.abort_flag = 1;
         if (w.status != nullptr && atomicCAS(w.status, 0, FB_ERR_TIMEOUT) == 0) w.status[1] = site;
         return false;
@@ -108,7 +109,7 @@ __device__ __forceinline__ bool wait_count(const volatile int* c, int target, co
   while (*c < target) {
     if ((++it & 15u) == 0) {
       if (*w.abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > w.limit_ns) {
         *w.abort_flag = 1;
         if (w.status != nullptr && atomicCAS(w.status, 0, FB_ERR_TIMEOUT) == 0) w.status[1] = site;
         return false;
@@ -120,10 +121,10 @@ __device__ __forceinline__ bool wait_count(const volatile int* c, int target, co
 
 // Time-bounded wait that ignores the abort flag: used on the abort path to let copies and MMAs
 // already in flight land before the CTA releases its shared and tensor memory.
-__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
   return true;
 }

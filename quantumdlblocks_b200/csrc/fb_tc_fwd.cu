@@ -113,6 +113,8 @@ struct FwdParams {
   int64_t o_s0, o_s1, o_s2;
   float* z;
   int* status;
+  uint64_t wait_limit_ns;  // bound of every wait
+  int skip_first_k;        // test hook: CTA 0 never issues its first K-tile copy
 };
 
 template <class Map> struct TcMap;
@@ -179,7 +181,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const WaitCtx wc{abort_flag, p.status};
+  const WaitCtx wc{abort_flag, p.status, p.wait_limit_ns};
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -253,6 +255,12 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
           if (g >= S) ok = mbar_wait(&empty[st], ((g / S) - 1) & 1, wc, 2 + 10 * lane);
           if (!ok) break;
           const int n0 = it.n_first + t * kBN;
+          if (lane == 0 && p.skip_first_k && blockIdx.x == 0 && g == 0) {
+            // test hook: this copy is never requested, so every wait on it runs into its bound
+            // and the CTA takes the abort path (fb_test_born_fwd_timeout)
+            issued = g + 1;
+            continue;
+          }
           mbar_arrive_expect_tx(&full[st], Cfg::kTileBytes);
 #pragma unroll
           for (int hf = 0; hf < Cfg::kHalves; ++hf)
@@ -265,8 +273,9 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       }
       if (!ok) {
         // abandoned: let this lane's copies already in flight land before the CTA exits
-        for (int gg = max(0, issued - S); gg < issued; ++gg) mbar_wait_drain(&full[gg % S], (gg / S) & 1);
-        for (int qq = max(0, q_issued - 2); qq < q_issued; ++qq) mbar_wait_drain(&q_full[qq & 1], (qq >> 1) & 1);
+        for (int gg = max(0, issued - S); gg < issued; ++gg) mbar_wait_drain(&full[gg % S], (gg / S) & 1, wc.limit_ns);
+        for (int qq = max(0, q_issued - 2); qq < q_issued; ++qq)
+          mbar_wait_drain(&q_full[qq & 1], (qq >> 1) & 1, wc.limit_ns);
       }
     }
     __syncwarp();
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       }
       if (!ok) {  // wait for this thread's products in flight before TMEM is released
         mma_commit(drain);
-        mbar_wait_drain(drain, 0);
+        mbar_wait_drain(drain, 0, wc.limit_ns);
       }
     }
     __syncwarp();
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       }
       if (!ok) {
         mma_commit(drain + 1);
-        mbar_wait_drain(drain + 1, 0);
+        mbar_wait_drain(drain + 1, 0, wc.limit_ns);
       }
     }
     __syncwarp();
@@ -687,6 +696,8 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   fp.o_s0 = pr.o.s[0]; fp.o_s1 = pr.o.s[1]; fp.o_s2 = pr.o.s[2];
   fp.z = pr.z;
   fp.status = pr.status;
+  fp.wait_limit_ns = pr.wait_limit_ns ? pr.wait_limit_ns : sm100::kWaitLimitNs;
+  fp.skip_first_k = pr.test_skip_first_k;
   int rc;
   if (pr.D == 64)
     rc = pr.purified ? fwd_doc<64, PurifiedMap>(pr, s, fp, mq, mk, mv) : fwd_doc<64, PlainMap>(pr, s, fp, mq, mk, mv);
