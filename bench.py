@@ -64,7 +64,8 @@ WORKLOADS = {
 # from an ncu capture of a named build: (bytes, source).  A static figure: a rebuilt kernel keeps
 # reporting it until it is profiled again, which is why its source names the profiled build.
 PROFILED_TRAFFIC = {
-    ("c2", "bwd"): (294.9e6, "static: ncu capture of tc_bwd_kernel at C2, build 6513c74"),
+    ("c2", "bwd"): (294.2e6, "static: ncu capture of tc_bwd_kernel at C2, build 4b9d2b0"),
+    ("c2", "fwd"): (133.5e6, "static: ncu capture of tc_fwd_kernel at C2, build 4b9d2b0"),
 }
 
 
@@ -316,6 +317,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         return
     if args.mode == "families":
         run_families_mode(args, rank, flush, dev, flops_step)
+        return
+    if args.mode == "triton-reference":
+        run_triton_reference_mode(args, rank, flush, dev, q, k, v, do, scale, doc, causal, flops_step)
         return
     if args.mode == "gpt":
         gpt = run_gpt(args, rank, world, dev)
@@ -763,6 +767,66 @@ def run_families_mode(args, rank: int, flush: torch.Tensor, dev: torch.device, f
                           "device_status": rc}), flush=True)
 
 
+def run_triton_reference_mode(args, rank, flush, dev, q, k, v, do, scale, doc, causal, flops_step) -> None:
+    """--mode triton-reference: the reference's own GPU path -- ``flash_born_attention`` of
+    qdlblocks (``kernels/flash_born.py:655-690``, Triton kernels ``:80-430``), unmodified, imported
+    from ``baseline/_ref`` -- forward + backward on this GPU at the workload's shape and inputs,
+    timed like the benchmark step (L2 flushed, CUDA events).  The bar on a B200 is that code
+    JIT-compiled for it.  The same inputs then run through this package's op and the two results
+    are compared (max-rel), so the figure is known to be of the same computation."""
+    from quantumdlblocks_b200 import flash_born_attention
+
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "qdlblocks")):
+        if rank == 0:
+            print(json.dumps({"mode": "triton-reference", "unavailable": "baseline/_ref holds no qdlblocks package"}))
+        return
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import warnings
+
+    warnings.filterwarnings("ignore")
+    from qdlblocks.kernels.flash_born import HAS_TRITON
+    from qdlblocks.kernels.flash_born import flash_born_attention as ref_attention
+
+    def grads(fn):
+        out = fn(q, k, v, scale, is_causal=causal, eps=1e-12, doc_ids=doc)
+        return (out, *torch.autograd.grad(out, (q, k, v, scale), do))
+
+    t0 = time.perf_counter()
+    grads(ref_attention)  # first call: Triton compiles its kernels for this GPU
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    for _ in range(args.warmup):
+        grads(ref_attention)
+    total = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda._sleep(16 * HEAD_START_CYCLES)  # the host queues the step before the timed region
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        grads(ref_attention)
+        a1.record()
+        torch.cuda.synchronize()
+        total += a0.elapsed_time(a1)
+    ms = total / args.steps
+    ref = grads(ref_attention)
+    ours = grads(flash_born_attention)
+    names = ("out", "dq", "dk", "dv")
+    diff = {n: float((a.float() - b.float()).abs().max() / b.float().abs().max().clamp_min(1e-30))
+            for n, a, b in zip(names, ours[:4], ref[:4])}
+    peaks, src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    tf = flops_step / (ms / 1e3) / 1e12
+    if rank == 0:
+        print(json.dumps({"mode": "triton-reference", "workload": args.workload, "has_triton": bool(HAS_TRITON),
+                          "ms_per_step": ms, "tflops": tf, "frac_bf16_peak": tf / peak,
+                          "peak_source": f"bf16_tflops (burst) of {src}", "first_call_s": compile_s,
+                          "max_rel_ours_vs_reference": diff,
+                          "what": "qdlblocks flash_born_attention (Triton) fwd + autograd bwd, unmodified, "
+                                  "from baseline/_ref"}), flush=True)
+
+
 def run_kernel_mode(args, q, k, v, do, scale, doc, causal, flops_step, D, pairs, flush, rank, world, dev) -> None:
     """--mode fwd|bwd: launch only the forward or only the backward kernels through the custom
     ops (one C-ABI call per step), W warm-up + K timed launches, for profilers and kernel timing."""
@@ -833,11 +897,13 @@ def main() -> None:
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-warmup", type=int, default=3)
     ap.add_argument("--gpt-batch", type=int, default=16)
-    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue", "families", "gpt"], default="step",
+    ap.add_argument("--mode", choices=["step", "fwd", "bwd", "prologue", "families", "gpt", "triton-reference"],
+                    default="step",
                     help="step: the benchmark (fwd+bwd); fwd / bwd: one kernel family only (profiling); "
                          "prologue: the attention layer's fused operand kernels at the C5 shape; "
                          "families: complex-phase and paired-heads attention at the C2 shape; "
-                         "gpt: only the C5 GPT training step")
+                         "gpt: only the C5 GPT training step; triton-reference: the reference's own Triton "
+                         "kernels (baseline/_ref) on this GPU, same inputs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
