@@ -629,6 +629,18 @@ __device__ __forceinline__ QItem q_item(const BwdParams& p, int idx) {
   return it;
 }
 
+// Global index of this CTA's j-th query-major item, or -1 when it has no more: rows of gridDim.x
+// items dealt left to right on even rows and right to left on odd ones (snake order), which keeps
+// every CTA's total within about one item of the others for items sorted heaviest first; with
+// document ids (sizes that follow the documents) every row is dealt left to right.
+__device__ __forceinline__ int q_slot(const BwdParams& p, int j) {
+  const int G = (int)gridDim.x;
+  const bool back = (j & 1) && p.doc_qr == nullptr;
+  const int idx = j * G + (back ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return idx < p.n_qitems ? idx : -1;
+}
+
+
 template <int D, class Map, bool kHasDoc>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmdO,
@@ -723,7 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         q_issued = item_seq + 1;
         return true;
       };
-      for (int idx = blockIdx.x; idx < p.n_qitems && ok; idx += gridDim.x, ++i) {
+      for (int idx = q_slot(p, 0); idx >= 0 && ok; idx = q_slot(p, i + 1), ++i) {
         const QItem it = q_item(p, idx);
         if (lane == 0 && q_issued <= i) ok = load_q(i, it);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
@@ -739,8 +751,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued = g + 1;
           // with two Q / dO buffers, the next item's are requested once this item's first key
           // tile is on its way
-          if (QB == 2 && lane == 0 && t == 0 && idx + (int)gridDim.x < p.n_qitems)
-            ok = load_q(i + 1, q_item(p, idx + gridDim.x));
+          if (QB == 2 && lane == 0 && t == 0 && q_slot(p, i + 1) >= 0)
+            ok = load_q(i + 1, q_item(p, q_slot(p, i + 1)));
         }
       }
       if (!ok) {
@@ -757,10 +769,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idS = idesc_f16(1, 0, 0, BN, C::kBM);  // M = 128 queries, N = 64 keys
       constexpr uint32_t idQ = idesc_f16(1, 0, 1, D, C::kBM);   // A TMEM (G), B MN-major (K), N = D
       bool ok = true;
-      int s_idx = blockIdx.x, s_i = 0, s_t = 0, s_g = 0;
-      int u_idx = blockIdx.x, u_i = 0, u_t = 0, u_g = 0;
+      int s_idx = q_slot(p, 0), s_i = 0, s_t = 0, s_g = 0;
+      int u_idx = q_slot(p, 0), u_i = 0, u_t = 0, u_g = 0;
       QItem s_it{}, u_it{};
-      bool s_have = s_idx < p.n_qitems, u_have = u_idx < p.n_qitems;
+      bool s_have = s_idx >= 0, u_have = u_idx >= 0;
       if (s_have) s_it = q_item(p, s_idx);
       if (u_have) u_it = q_item(p, u_idx);
       // which = 0: S = Q K^T into S[b]; which = 1: dP = dO V^T into dP[b]
@@ -790,8 +802,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++s_t == s_it.n_count) {
           s_t = 0;
           ++s_i;
-          s_idx += gridDim.x;
-          s_have = s_idx < p.n_qitems;
+          s_idx = q_slot(p, s_i);
+          s_have = s_idx >= 0;
           if (s_have) s_it = q_item(p, s_idx);
         }
         return true;
@@ -814,8 +826,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++u_t == u_it.n_count) {
           u_t = 0;
           ++u_i;
-          u_idx += gridDim.x;
-          u_have = u_idx < p.n_qitems;
+          u_idx = q_slot(p, u_i);
+          u_have = u_idx >= 0;
           if (u_have) u_it = q_item(p, u_idx);
         }
         return true;
@@ -857,8 +869,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       dlz_n = zd.y;
       if constexpr (kHasDoc) doc_n = q < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)q * p.doc_s1] : -1;
     };
-    if (blockIdx.x < p.n_qitems) fetch(blockIdx.x);
-    for (int idx = blockIdx.x; idx < p.n_qitems && ok; idx += gridDim.x, ++i) {
+    if (q_slot(p, 0) >= 0) fetch(q_slot(p, 0));
+    for (int idx = q_slot(p, 0); idx >= 0 && ok; idx = q_slot(p, i + 1), ++i) {
       const QItem it = it_n;
       const Map map = map_n;
       const int doc_i = doc_n;
@@ -921,7 +933,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&g_full[b]);
       }
       if (!ok) break;
-      if (idx + (int)gridDim.x < p.n_qitems) fetch(idx + gridDim.x);
+      if (q_slot(p, i + 1) >= 0) fetch(q_slot(p, i + 1));
       // ---- epilogue of the item: dQ rows (group wg stores head-dim columns [wg D/2, (wg+1) D/2))
       ok = __all_sync(0xffffffffu, mbar_wait(dq_full, i & 1, wc, 51));
       if (!ok) break;

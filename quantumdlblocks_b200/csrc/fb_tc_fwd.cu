@@ -1,7 +1,7 @@
 // fb_tc_fwd.cu -- flash-Born forward on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // Persistent kernel: one CTA per SM walks work items (batch, head, 128-query tile), heaviest
-// first (longest-processing-time order for the causal mask), round-robin over CTAs.  Each item
+// first (longest-processing-time order for the causal mask), dealt out in snake order.  Each item
 // walks the key tiles (128 keys) that can hold valid pairs (causal / window tile skipping, as
 // flash_born.py:152-156).  The tile sequence is flattened across items, so the TMA ring, the
 // TMEM double buffers and the mbarrier phases run on from one item into the next and the
@@ -151,6 +151,20 @@ __device__ __forceinline__ Item item_at(const FwdParams& p, int idx) {
   return it;
 }
 
+// Global index of this CTA's j-th work item, or -1 when it has no more.  The items (sorted
+// heaviest first by item_at) are dealt out in rows of gridDim.x, left to right on even rows and
+// right to left on odd ones (snake order): every CTA's total stays within about one item of the
+// others, where dealing every row left to right hands the first CTAs the heaviest item of each
+// row (C2: the busiest CTA 119 key tiles against 125, the mean being 117.6; a quarter of C2's
+// heads: 31 against 38).  With document ids the item sizes follow the documents, not the order,
+// and every row is dealt left to right (measured faster at C4).
+__device__ __forceinline__ int fwd_slot(const FwdParams& p, int j) {
+  const int G = (int)gridDim.x;
+  const bool back = (j & 1) && p.doc_qr == nullptr;
+  const int idx = j * G + (back ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  return idx < p.n_items ? idx : -1;
+}
+
 template <int D, class Map, bool kHasDoc, typename TO>
 __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -246,7 +260,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
         q_issued = item_seq + 1;
         return true;
       };
-      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      for (int idx = fwd_slot(p, 0); idx >= 0 && ok; idx = fwd_slot(p, i + 1), ++i) {
         const Item it = item_at(p, idx);
         if (lane == 0 && q_issued <= i) ok = load_q(i, it);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
@@ -268,7 +282,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                           it.b, p.H);
           issued = g + 1;
           // once the first K of this item is on its way, fetch the next item's Q
-          if (lane == 0 && t == 0 && idx + (int)gridDim.x < p.n_items) ok = load_q(i + 1, item_at(p, idx + gridDim.x));
+          if (lane == 0 && t == 0 && fwd_slot(p, i + 1) >= 0) ok = load_q(i + 1, item_at(p, fwd_slot(p, i + 1)));
         }
       }
       if (!ok) {
@@ -285,7 +299,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       constexpr uint32_t idS = idesc_f16(1, 0, 0, kBN, kBM);  // S: A K-major, B K-major, N = 128
       bool ok = true;
       int g = 0, i = 0;
-      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      for (int idx = fwd_slot(p, 0); idx >= 0 && ok; idx = fwd_slot(p, i + 1), ++i) {
         const Item it = item_at(p, idx);
         ok = mbar_wait(&q_full[i & 1], (i >> 1) & 1, wc, 3);
         const uint32_t q_base = smem_u32(smem + Cfg::kQOff + (i & 1) * Cfg::kTileBytes);
@@ -322,7 +336,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       const uint32_t ones_base = smem_u32(smem + Cfg::kOnesOff);
       bool ok = true;
       int g = 0, i = 0;
-      for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+      for (int idx = fwd_slot(p, 0); idx >= 0 && ok; idx = fwd_slot(p, i + 1), ++i) {
         const Item it = item_at(p, idx);
         for (int t = 0; t < it.n_count && ok; ++t, ++g) {
           const int st = g % S;
@@ -365,7 +379,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(lg * 32) << 16);
     bool ok = true;
     int i = 0;
-    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+    for (int idx = fwd_slot(p, 0); idx >= 0 && ok; idx = fwd_slot(p, i + 1), ++i) {
       const Item it = item_at(p, idx);
       const int qi = it.m0 + row;
       static_assert(!Cfg::kEpiWarps || Cfg::kTcZ, "the epilogue warpgroup reads Z from TMEM");
@@ -430,8 +444,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
         doc_n = q < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)q * p.doc_s1] : -1;
       }
     };
-    if (blockIdx.x < p.n_items) fetch(blockIdx.x);
-    for (int idx = blockIdx.x; idx < p.n_items && ok; idx += gridDim.x, ++i) {
+    if (fwd_slot(p, 0) >= 0) fetch(fwd_slot(p, 0));
+    for (int idx = fwd_slot(p, 0); idx >= 0 && ok; idx = fwd_slot(p, i + 1), ++i) {
       const Item it = it_n;
       const Map map = map_n;
       const int doc_i = doc_n;
@@ -553,7 +567,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
         tc_fence_before();
         mbar_arrive(&p_full[wg]);
       }
-      if (idx + (int)gridDim.x < p.n_items) fetch(idx + gridDim.x);
+      if (fwd_slot(p, i + 1) >= 0) fetch(fwd_slot(p, i + 1));
       if constexpr (Cfg::kEpiWarps) {  // the epilogue warpgroup takes the item's O; go straight on
         g += it.n_count;
         continue;
