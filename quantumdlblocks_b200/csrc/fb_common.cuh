@@ -164,7 +164,9 @@ __host__ __device__ inline int doc_blocks(int T) { return (T + kDocBlock - 1) / 
 struct DocRanges {
   const int2* qr;
   const int2* kr;
-  const int2* mm;  // per 64-row block (min, max) document id
+  const int2* mm;    // per 64-row block (min, max) document id
+  const int2* runs;  // [B][T] positions [first, last + 1) holding each position's id (rows with mono = 1)
+  const int* mono;   // [B] 1 when the row's ids never decrease along the sequence
   int nblk;
 };
 

@@ -103,6 +103,8 @@ struct BwdParams {
   int map3;            // tensor maps address (b, h) as one merged dimension
   const int2* doc_kr;  // document spans of the key blocks (null without document ids)
   const int2* doc_mm;  // per-block (min, max) document ids
+  const int2* doc_runs;  // [B][T] run of equal ids around each position (rows with doc_mono = 1)
+  const int* doc_mono;   // [B] the row's ids never decrease
   int nblk;
   int* status;
 };
@@ -457,12 +459,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     BwdItem it_n;
     bool have_n = bwd_next(p, k, it_n);
     Map map_n{};
-    int doc_n = 0;
+    int doc_n = 0, mono_n = 0;
+    int2 run_n = make_int2(0, 0);
     auto fetch = [&]() {
       map_n = BwdMap<Map>::make(p, it_n.h);
       if constexpr (kHasDoc) {
         const int kr = it_n.n0 + jr;
         doc_n = kr < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)kr * p.doc_s1] : -2;
+        mono_n = p.doc_mono[it_n.b];
+        if (kr < p.T) run_n = p.doc_runs[(int64_t)it_n.b * p.T + kr];
       }
     };
     if (have_n) fetch();
@@ -471,6 +476,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Map map = map_n;
       const int doc_j = doc_n;
       (void)doc_j;
+      // Rows whose document ids never decrease (packed documents) mask by the key's run of equal
+      // ids, folded into the valid query-column range; other rows compare ids pair by pair.
+      const bool cmp = kHasDoc && mono_n == 0;
+      const int2 run_j = run_n;
+      (void)run_j;
       const int64_t bh = (int64_t)it.b * p.H + it.h;
       const int n0 = it.n0;
       const int kj = n0 + jr;
@@ -479,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int gg = g + t;  // gg % 2 == wg
         const int sb = wg;
         const int m0 = it.m_first + t * kBM;
-        if constexpr (kHasDoc) {
+        if (cmp) {
 #pragma unroll
           for (int u = 0; u < kBM / 32; ++u) {
             const int qi = m0 + u * 32 + lane;
@@ -505,15 +515,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Partial tiles: the raw score of every invalid pair is replaced by NaN before the map,
         // which turns it into p = 0 and dL/draw = 0 (fmaxf returns its non-NaN operand and no
         // other term of these maps touches raw), so one branch-free body serves every tile.
-        const int lo_q = p.causal ? kj - m0 : -kBM;  // causal: query column qx is valid iff qx >= kj - m0
-        const int hi_q = kj < p.T ? p.T - m0 : 0;    // queries below T; a padded key row has none
+        int lo_q = p.causal ? kj - m0 : -kBM;  // causal: query column qx is valid iff qx >= kj - m0
+        int hi_q = kj < p.T ? p.T - m0 : 0;    // queries below T; a padded key row has none
+        if (!cmp) {  // the window (i - j < window) and the key's document run as bounds of the range
+          if (p.window > 0) hi_q = min(hi_q, kj + p.window - m0);
+          if constexpr (kHasDoc) {
+            lo_q = max(lo_q, run_j.x - m0);
+            hi_q = min(hi_q, run_j.y - m0);
+          }
+        }
         auto mask16 = [&](int sc, uint32_t (&rs)[16]) {
+          if (kHasDoc && cmp) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int qx = sc * 16 + e;
-            bool v = (qx >= lo_q) & (qx < hi_q) & ((p.window <= 0) | ((m0 + qx) - kj < p.window));
-            if constexpr (kHasDoc) v = v & (docq[qx] == doc_j);
-            rs[e] = v ? rs[e] : 0x7FC00000u;
+            for (int e = 0; e < 16; ++e) {
+              const int qx = sc * 16 + e;
+              const bool v = (qx >= lo_q) & (qx < hi_q) & ((p.window <= 0) | ((m0 + qx) - kj < p.window)) &
+                             (docq[qx] == doc_j);
+              rs[e] = v ? rs[e] : 0x7FC00000u;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int qx = sc * 16 + e;
+              rs[e] = (qx >= lo_q) & (qx < hi_q) ? rs[e] : 0x7FC00000u;
+            }
           }
         };
         // one 16-query sub-chunk: W, G -> TMEM (over consumed columns), G -> smem
@@ -969,6 +994,8 @@ int tc_bwd64(const Problem& pr, cudaStream_t s, int* launches) {
   if (drc != FB_OK) return drc;
   bp.doc_kr = dr.kr;
   bp.doc_mm = dr.mm;
+  bp.doc_runs = dr.runs;
+  bp.doc_mono = dr.mono;
   bp.nblk = dr.nblk;
 
   CUtensorMap mdq;

@@ -108,6 +108,8 @@ struct FwdParams {
   int64_t doc_s0, doc_s1;
   const int2* doc_qr;  // document spans of the query blocks (null without document ids)
   const int2* doc_mm;  // per-block (min, max) document ids
+  const int2* doc_runs;  // [B][T] run of equal ids around each position (rows with doc_mono = 1)
+  const int* doc_mono;   // [B] the row's ids never decrease
   int nblk;
   void* out;
   int64_t o_s0, o_s1, o_s2;
@@ -435,13 +437,16 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
     // the next item are requested before the current item's epilogue, which hides their latency.
     Item it_n{};
     Map map_n{};
-    int doc_n = 0;
+    int doc_n = 0, mono_n = 0;
+    int2 run_n = make_int2(0, 0);
     auto fetch = [&](int idx) {
       it_n = item_at(p, idx);
       map_n = TcMap<Map>::make(p, it_n.h);
       if constexpr (kHasDoc) {
         const int q = it_n.m0 + row;
         doc_n = q < p.T ? p.doc[(int64_t)it_n.b * p.doc_s0 + (int64_t)q * p.doc_s1] : -1;
+        mono_n = p.doc_mono[it_n.b];
+        run_n = q < p.T ? p.doc_runs[(int64_t)it_n.b * p.T + q] : make_int2(0, 0);
       }
     };
     if (fwd_slot(p, 0) >= 0) fetch(fwd_slot(p, 0));
@@ -451,11 +456,23 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       const int doc_i = doc_n;
       const int qi = it.m0 + row;
       (void)doc_i;
+      // This row's valid keys as one range [klo, khi): causal, window and T always; with document
+      // ids whose row never decreases (packed documents), the row's run of equal ids too.  Other
+      // rows with document ids compare ids pair by pair (cmp).
+      const bool cmp = kHasDoc && mono_n == 0;
+      int klo = p.window > 0 ? qi - p.window + 1 : 0;
+      int khi = p.causal ? min(p.T, qi + 1) : p.T;
+      if constexpr (kHasDoc) {
+        if (!cmp) {
+          klo = max(klo, run_n.x);
+          khi = min(khi, run_n.y);
+        }
+      }
       float zsum = 0.f;
       for (int t = (wg - g) & 1; t < it.n_count && ok; t += 2) {
         const int gg = g + t;  // gg % 2 == wg
         const int n0 = it.n_first + t * kBN;
-        if constexpr (kHasDoc) {
+        if (cmp) {
 #pragma unroll
           for (int u = 0; u < kBN / 32; ++u) {
             const int kj = n0 + u * 32 + lane;
@@ -536,31 +553,48 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
             }
             tmem_st16(p_addr + c * 16, w);
           }
-        } else {
-          // Compact loop (not unrolled over chunks): keeps the masked variant small in the
+        } else if (!cmp) {
+          // Compact loops (not unrolled over chunks) keep the masked variants small in the
           // instruction cache (a fully unrolled 128-column body with both variants does not fit).
+          // Key column e of chunk c is valid iff klo <= n0 + 32 c + e < khi.
 #pragma unroll 1
           for (int c = 0; c < kBN / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(s_addr + c * 32, r);
             tmem_wait_ld();
             uint32_t w[16];
-            const int kbase = n0 + c * 32;
-            const int* dk = docs_k + c * 32;
+            const int lo = klo - (n0 + c * 32), hi = khi - (n0 + c * 32);
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-              float pr[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                int doc_j = 0;
-                if constexpr (kHasDoc) doc_j = dk[e + u];
-                const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, doc_j);
-                pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
-              }
-              w[e / 2] = pack2<true>(pr[0], pr[1]);
+              w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), (e >= lo) & (e < hi)),
+                                     map.prob(__uint_as_float(r[e + 1]), (e + 1 >= lo) & (e + 1 < hi)));
               if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
             }
             tmem_st16(p_addr + c * 16, w);
+          }
+        } else {
+          if constexpr (kHasDoc) {
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(s_addr + c * 32, r);
+              tmem_wait_ld();
+              uint32_t w[16];
+              const int kbase = n0 + c * 32;
+              const int* dk = docs_k + c * 32;
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float pr[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                  const bool valid = pair_valid(qi, kbase + e + u, p.T, p.causal, p.window, doc_i, dk[e + u]);
+                  pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
+                }
+                w[e / 2] = pack2<true>(pr[0], pr[1]);
+                if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+              }
+              tmem_st16(p_addr + c * 16, w);
+            }
           }
         }
         tmem_wait_st();
@@ -705,6 +739,8 @@ int tc_fwd(const Problem& pr, cudaStream_t s, int* launches) {
   if (drc != FB_OK) return drc;
   fp.doc_qr = dr.qr;
   fp.doc_mm = dr.mm;
+  fp.doc_runs = dr.runs;
+  fp.doc_mono = dr.mono;
   fp.nblk = dr.nblk;
   fp.out = const_cast<void*>(pr.o.ptr);
   fp.o_s0 = pr.o.s[0]; fp.o_s1 = pr.o.s[1]; fp.o_s2 = pr.o.s[2];

@@ -29,8 +29,25 @@ def _fwd(q, k, v, scale, tau, doc, causal, window, purified, path):
     return out, z, launches
 
 
+def make_docs(rng, B, T, doc_mean):
+    """Document ids: doc_mean > 0 packs documents of geometric length (ids rising along the
+    sequence, as the reference's running count of end-of-text tokens gives); doc_mean < 0 packs
+    row 0 that way and gives the other rows runs of ids drawn from {0, 1, 2}, so one id comes back
+    after others (the kernels then compare ids pair by pair instead of using runs)."""
+    if doc_mean is None:
+        return None
+    doc = np.zeros((B, T), np.int32)
+    for b in range(B):
+        t, d = 0, 0
+        while t < T:
+            L = int(rng.geometric(1 / abs(doc_mean)))
+            doc[b, t:t + L] = d if (doc_mean > 0 or b == 0) else int(rng.integers(0, 3))
+            t, d = t + L, d + 1
+    return doc
+
+
 CASES = [
-    # B, H, T, D, causal, window, doc_mean
+    # B, H, T, D, causal, window, doc_mean (negative: ids that come back, see make_docs)
     (1, 1, 128, 64, True, 0, None),
     (1, 2, 1, 64, True, 0, None),
     (2, 2, 77, 64, True, 0, None),
@@ -44,6 +61,11 @@ CASES = [
     # long documents: most tiles lie inside one document and take the unmasked fast path
     (2, 2, 1500, 64, True, 0, 600.0),
     (1, 2, 1100, 128, True, 0, 500.0),
+    # documents with a window, without the causal mask, and ids that come back in a later run
+    (2, 2, 800, 64, True, 200, 150.0),
+    (2, 2, 600, 64, False, 0, 150.0),
+    (2, 2, 900, 64, True, 0, -120.0),
+    (2, 2, 700, 128, True, 0, -80.0),
 ]
 
 
@@ -57,15 +79,7 @@ def test_tc_forward_matches_oracle_and_general(case, purified):
         q /= np.linalg.norm(q, axis=-1, keepdims=True)
         k /= np.linalg.norm(k, axis=-1, keepdims=True)
     q, k, v = (round_to(x, torch.bfloat16) for x in (q, k, v))
-    doc = None
-    if doc_mean is not None:
-        doc = np.zeros((B, T), np.int32)
-        for b in range(B):
-            t, d = 0, 0
-            while t < T:
-                L = int(rng.geometric(1 / doc_mean))
-                doc[b, t:t + L] = d
-                t, d = t + L, d + 1
+    doc = make_docs(rng, B, T, doc_mean)
     scale = np.linspace(6.0, 9.0, H).astype(np.float32) if purified else np.linspace(0.3, 0.5, H).astype(np.float32)
     tau = np.linspace(0.02, 0.08, H).astype(np.float32) if purified else None
     dev = "cuda"
@@ -137,15 +151,7 @@ def test_tc_backward_matches_oracle(case, purified, deterministic):
         q /= np.linalg.norm(q, axis=-1, keepdims=True)
         k /= np.linalg.norm(k, axis=-1, keepdims=True)
     q, k, v, do = (round_to(x, torch.bfloat16) for x in (q, k, v, do))
-    doc = None
-    if doc_mean is not None:
-        doc = np.zeros((B, T), np.int32)
-        for b in range(B):
-            t, d = 0, 0
-            while t < T:
-                L = int(rng.geometric(1 / doc_mean))
-                doc[b, t:t + L] = d
-                t, d = t + L, d + 1
+    doc = make_docs(rng, B, T, doc_mean)
     scale = np.linspace(6.0, 9.0, H).astype(np.float32) if purified else np.linspace(0.3, 0.5, H).astype(np.float32)
     kw = dict(is_causal=causal, window_size=window, doc_ids=doc)
     if purified:
