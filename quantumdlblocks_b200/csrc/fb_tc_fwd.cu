@@ -468,7 +468,10 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
           khi = min(khi, run_n.y);
         }
       }
-      float zsum = 0.f;
+      // d=128: row sum of the bf16-rounded p, in two independent packed-pair chains (a single
+      // running sum would serialise 128 dependent adds per tile)
+      f32x2 zacc[2] = {f2_make(0.f, 0.f), f2_make(0.f, 0.f)};
+      auto zadd = [&](int e2, uint32_t wv) { zacc[e2 & 1] = f2_add(zacc[e2 & 1], f2_make(bf16_lo(wv), bf16_hi(wv))); };
       for (int t = (wg - g) & 1; t < it.n_count && ok; t += 2) {
         const int gg = g + t;  // gg % 2 == wg
         const int n0 = it.n_first + t * kBN;
@@ -517,7 +520,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
               } else {
                 w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), true), map.prob(__uint_as_float(r[e + 1]), true));
               }
-              if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+              if constexpr (!Cfg::kTcZ) zadd(e / 2, w[e / 2]);
             }
             tmem_st16(p_addr + c * 16, w);
           };
@@ -548,7 +551,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
               for (int e = 0; e < 32; e += 2) {
                 w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), e <= lim),
                                        map.prob(__uint_as_float(r[e + 1]), e + 1 <= lim));
-                if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+                if constexpr (!Cfg::kTcZ) zadd(e / 2, w[e / 2]);
               }
             }
             tmem_st16(p_addr + c * 16, w);
@@ -568,7 +571,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
             for (int e = 0; e < 32; e += 2) {
               w[e / 2] = pack2<true>(map.prob(__uint_as_float(r[e]), (e >= lo) & (e < hi)),
                                      map.prob(__uint_as_float(r[e + 1]), (e + 1 >= lo) & (e + 1 < hi)));
-              if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+              if constexpr (!Cfg::kTcZ) zadd(e / 2, w[e / 2]);
             }
             tmem_st16(p_addr + c * 16, w);
           }
@@ -591,7 +594,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
                   pr[u] = map.prob(__uint_as_float(r[e + u]), valid);
                 }
                 w[e / 2] = pack2<true>(pr[0], pr[1]);
-                if constexpr (!Cfg::kTcZ) zsum += bf16_lo(w[e / 2]) + bf16_hi(w[e / 2]);
+                if constexpr (!Cfg::kTcZ) zadd(e / 2, w[e / 2]);
               }
               tmem_st16(p_addr + c * 16, w);
             }
@@ -609,7 +612,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, 1)
       // ---- epilogue of the item (d = 128): Z (the two groups' row sums), O * (1 / Z)
       float* zp = zpart + (i & 1) * 2 * kBM;
       if constexpr (!Cfg::kTcZ) {
-        zp[wg * kBM + row] = zsum;
+        zp[wg * kBM + row] = (f2_lo(zacc[0]) + f2_hi(zacc[0])) + (f2_lo(zacc[1]) + f2_hi(zacc[1]));
         mbar_arrive(z_bar);
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(z_bar, i & 1, wc, 10));
       }
