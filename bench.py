@@ -64,8 +64,8 @@ WORKLOADS = {
 # from an ncu capture of a named build: (bytes, source).  A static figure: a rebuilt kernel keeps
 # reporting it until it is profiled again, which is why its source names the profiled build.
 PROFILED_TRAFFIC = {
-    ("c2", "bwd"): (294.2e6, "static: ncu capture of tc_bwd_kernel at C2, build 4b9d2b0"),
-    ("c2", "fwd"): (133.5e6, "static: ncu capture of tc_fwd_kernel at C2, build 4b9d2b0"),
+    ("c2", "bwd"): (294.6e6, "static: ncu capture of tc_bwd_kernel at C2, build b5a6055"),
+    ("c2", "fwd"): (130.6e6, "static: ncu capture of tc_fwd_kernel at C2, build b5a6055"),
 }
 
 
