@@ -17,6 +17,9 @@ problem of its own instead (weak scaling); the strong run also reports that figu
 FLOPs are algorithmic: 14 d per valid (query, key) pair (forward QK^T and PV, backward S
 recompute, dP, dV, dK, dQ), elementwise work not counted.
 
+With the default C2 workload the run also times C3 and C4 the same way (split over the ranks,
+``--extra-steps`` steps each) and reports them under ``"workloads"``.
+
 The same run then times the end-to-end data-parallel training step of the C5 GPT (d_model 1024,
 6 layers, flash-Born attention, per-GPU batch 16 x 1024 tokens; NCCL gradient all-reduce across
 the N ranks) and reports it under ``"gpt"`` in tokens/s (``--no-gpt`` skips it).
@@ -496,6 +499,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     traffic, traffic_src = profiled_traffic(args.workload, dominant)
 
+    others = None
+    if args.workload == "c2" and not args.weak and args.extra_steps > 0:
+        others = {w: run_other_workload(args, w, rank, world, dev, flush, peaks) for w in ("c3", "c4")}
+
     gpt = None if args.no_gpt else run_gpt(args, rank, world, dev)
 
     cpu = None
@@ -548,12 +555,97 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                     "copies": "pinned host buffers; H2D and D2H on two copy streams, pipelined across steps"},
             "gpu_launches": gpu_launches,
             "cpu_baseline": cpu,
+            "workloads": others,
             "gpt": gpt,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_other_workload(args, workload: str, rank: int, world: int, dev: torch.device, flush: torch.Tensor,
+                       peaks: dict) -> dict:
+    """C3 or C4 timed inside the default run, split over the ranks like the headline problem
+    (C3: 32 heads, 4 per GPU at N = 8; C4: heads split): ``--extra-steps`` fwd+bwd steps after two
+    warm-up steps, L2 flushed before each, CUDA events on this rank's stream, max over ranks;
+    then the forward and backward launches timed separately (C-ABI through the custom ops)."""
+    import torch.distributed as dist
+
+    from quantumdlblocks_b200 import flash_born_attention
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+    from quantumdlblocks_b200.sharding import max_over_ranks, plan_shards
+
+    B, H, N, D, causal, desc = WORKLOADS[workload]
+    q_cpu, k_cpu, v_cpu, do_cpu, doc_np, scale_val = make_inputs(workload, 0)
+    pairs_full = valid_pairs(workload, B, H, N, doc_np)
+    shard = plan_shards(B, H, N, world, is_causal=causal, doc_ids=doc_np)[rank]
+    bs, hs = slice(shard.b0, shard.b1), slice(shard.h0, shard.h1)
+    bf = torch.bfloat16
+    q, k, v = (x[bs, hs].to(bf).to(dev).requires_grad_(True) for x in (q_cpu, k_cpu, v_cpu))
+    do = do_cpu[bs, hs].to(bf).to(dev)
+    del q_cpu, k_cpu, v_cpu, do_cpu
+    doc = None if doc_np is None else torch.from_numpy(np.ascontiguousarray(doc_np[bs])).to(dev)
+    Hl = q.shape[1]
+    scale = torch.full((1, Hl, 1, 1), scale_val, device=dev, requires_grad=True)
+    pairs = valid_pairs(workload, q.shape[0], Hl, N, None if doc_np is None else doc_np[bs])
+
+    def step():
+        out = flash_born_attention(q, k, v, scale, is_causal=causal, eps=1e-12, doc_ids=doc)
+        torch.autograd.grad(out, (q, k, v, scale), do)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = args.extra_steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda._sleep(steps * HEAD_START_CYCLES)
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    sc_flat = scale.detach().reshape(-1).float().contiguous()
+    qd, kd, vd = q.detach(), k.detach(), v.detach()
+    t_fwd = t_bwd = 0.0
+    for _ in range(3):
+        flush.zero_()
+        torch.cuda._sleep(HEAD_START_CYCLES)
+        a0, a1, b0, b1 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+        a0.record()
+        out_d, z_d = torch.ops.flashborn_b200.born_fwd(qd, kd, vd, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+        a1.record()
+        flush.zero_()
+        b0.record()
+        torch.ops.flashborn_b200.born_bwd(do, qd, kd, vd, out_d, z_d, sc_flat, None, doc, causal, 1e-12, 0, 0.0, False)
+        b1.record()
+        torch.cuda.synchronize()
+        t_fwd += a0.elapsed_time(a1) / 3
+        t_bwd += b0.elapsed_time(b1) / 3
+    rc, site = fbm.device_status()
+    if rc != 0:
+        raise RuntimeError(f"device status {rc} (site {site}) in {workload}")
+    t_ms, t_fwd, t_bwd = max_over_ranks([t_ms, t_fwd, t_bwd], device=dev)
+    value = 14.0 * D * pairs_full * steps / (t_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    bwd_tf = 10.0 * D * pairs / (t_bwd / 1e3) / 1e12  # this rank's shard (the slowest rank's time)
+    res = {"metric": "born_attn_fwd_bwd_tflops", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+           "per_gpu_tflops": value / world, "ms_per_step": t_ms / steps, "steps": steps, "warmup": 2,
+           "scaling": "strong",
+           "config": {"workload": desc, "seq_len": N, "heads": H, "head_dim": D,
+                      "parallelism": f"(batch, head) units split over {world} ranks, rank 0 holds batch "
+                                     f"[{shard.b0},{shard.b1}) x heads [{shard.h0},{shard.h1}); no collective",
+                      "flops_per_step_job": 14.0 * D * pairs_full,
+                      "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush"},
+           "fwd_ms": t_fwd, "bwd_ms": t_bwd, "bwd_tflops_per_gpu": bwd_tf, "bwd_frac": bwd_tf / peak,
+           "peak_source": "bf16_tflops (burst), measured"}
+    del q, k, v, do, doc, scale, qd, kd, vd, out_d, z_d
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_gpt(args, rank: int, world: int, dev: torch.device) -> dict:
@@ -894,6 +986,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpt", action="store_true", help="skip the C5 GPT training-step measurement")
+    ap.add_argument("--extra-steps", type=int, default=5,
+                    help="steps of C3 and C4 timed in the default C2 run (0 skips them)")
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-warmup", type=int, default=3)
     ap.add_argument("--gpt-batch", type=int, default=16)
