@@ -5,7 +5,10 @@
 
 One step = one forward + backward of Born attention over one batch of synthetic inputs resident
 in HBM (C2: B=8, H=16, N=2048, d=64, bf16, causal, per-head scale 8, eps 1e-12; Q, K, V from
-torch seed 0, dO from seed 1, drawn in fp32 then cast).  With N GPUs (one process per GPU,
+torch seed 0, dO from seed 1, drawn in fp32 then cast).  The timed steps replay one captured
+step (public-API forward + autograd backward) as a CUDA graph, so a small shard's device time is
+not hidden behind the host's per-step Python work; ``eager_ms_per_step`` gives the eager figure
+(``--eager`` times eagerly throughout).  With N GPUs (one process per GPU,
 launched by torch.distributed.run) the one problem is split over the ranks (strong scaling):
 every rank takes a rectangle of its (batch, head) units from sharding.plan_shards -- C2's 128
 units become 64 / 32 / 16 per GPU at N = 2 / 4 / 8 (heads split), C3's 32 heads 4 per GPU at
@@ -191,6 +194,39 @@ def physical_gpu_index(local_rank: int) -> int:
     return local_rank
 
 
+def gpu_local_cpus(gpu_index: int) -> set[int] | None:
+    """The host CPUs NVML reports as local to a GPU (its NUMA node), or None when unknown."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:  # noqa: BLE001 -- no NVML, no GPU, no affinity support
+        return None
+
+
+def pinned_near_gpu(gpu_index: int, tensors):
+    """Pinned host copies of ``tensors``, allocated by this thread while it runs on the GPU's
+    local CPUs, so the pages sit on the GPU's NUMA node (a remote node halves the copy rate on
+    multi-socket hosts); the thread's CPU set is restored afterwards."""
+    cpus = gpu_local_cpus(gpu_index)
+    old = os.sched_getaffinity(0) if cpus else None
+    try:
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return [t.pin_memory() for t in tensors]
+    finally:
+        if old is not None:
+            os.sched_setaffinity(0, old)
+
+
 def cpu_eager_sample(workload: str, target_s: float, max_units: int | None = None):
     """Time the reference's CPU eager algorithm on whole (batch, head) units of the workload.
 
@@ -339,27 +375,46 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if rc != 0:
         raise RuntimeError(f"device status {rc} (site {site}) after warm-up")
 
+    # The timed steps replay one captured step (the public API's forward + autograd backward, the
+    # same kernels and allocations as an eager step) as a CUDA graph: a small shard's step (C2 at
+    # N = 8: ~75 us of device work) is shorter than the host's ~0.2 ms of Python, ctypes and
+    # autograd work per step, which eager timing would measure instead.  The eager per-step time
+    # is reported beside it.
+    graph, graph_err = (None, "disabled by --eager") if args.eager else capture_step(lambda: step(q, k, v, do), dev)
+
+    def timed_steps(n: int, use_graph: bool) -> float:
+        ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        barrier()
+        torch.cuda.synchronize()
+        # A device-side delay ahead of the timed steps lets the host queue them up, so that short
+        # runs (a few steps) time the device work rather than the host's first launches; it lies
+        # outside every per-step event pair.
+        torch.cuda._sleep(min(n, 200) * HEAD_START_CYCLES)
+        for i in range(n):
+            flush.zero_()  # L2 flush (256 MiB > 126 MB L2), outside the per-step events
+            ev_s[i].record()
+            if use_graph:
+                graph.replay()
+            else:
+                step(q, k, v, do)
+            ev_e[i].record()
+        torch.cuda.synchronize()
+        barrier()
+        return float(sum(ev_s[i].elapsed_time(ev_e[i]) for i in range(n)))
+
     sampler = ClockSampler(physical_gpu_index(local_rank))
     sampler.start()
     time.sleep(0.3)
-    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
-    # A device-side delay ahead of the timed steps lets the host queue them up, so that short runs
-    # (a few steps) time the device work rather than the host's first launches; it lies outside
-    # every per-step event pair.
-    torch.cuda._sleep(min(args.steps, 200) * HEAD_START_CYCLES)
-    for i in range(args.steps):
-        flush.zero_()  # L2 flush (256 MiB > 126 MB L2), outside the per-step events
-        ev_s[i].record()
-        step(q, k, v, do)
-        ev_e[i].record()
-    torch.cuda.synchronize()
-    barrier()
+    t_ms = timed_steps(args.steps, graph is not None)
     clocks = sampler.stop()
-    step_ms = [ev_s[i].elapsed_time(ev_e[i]) for i in range(args.steps)]
-    t_ms = float(sum(step_ms))
+    eager_steps = max(3, min(args.steps, 50))
+    if graph is not None:
+        for _ in range(2):  # untimed: eager allocations after the graph's private pool was taken
+            step(q, k, v, do)
+        t_eager = timed_steps(eager_steps, False)
+    else:
+        t_eager = t_ms * eager_steps / args.steps
     gpu_launches = args.steps * (launches["fwd"] + launches["bwd"])
 
     # per-kernel timing of the forward and backward launches (C-ABI through the custom ops)
@@ -396,8 +451,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     # results stream out while step i computes; every byte still crosses PCIe inside the timed
     # region, which ends when the last step's results are on the host.
     e2e_steps = max(3, min(args.steps, args.e2e_steps))
-    hq, hk, hv, hdo = (x.to(bf).pin_memory() for x in (q_cpu, k_cpu, v_cpu, do_cpu))
-    h_out = [[torch.empty_like(hq).pin_memory() for _ in range(4)] for _ in range(2)]
+    gpu_index = physical_gpu_index(local_rank)
+    hq, hk, hv, hdo = pinned_near_gpu(gpu_index, [x.to(bf) for x in (q_cpu, k_cpu, v_cpu, do_cpu)])
+    h_out = [pinned_near_gpu(gpu_index, [torch.empty_like(hq) for _ in range(4)]) for _ in range(2)]
     slots = [[torch.empty(hq.shape, dtype=bf, device=dev) for _ in range(4)] for _ in range(2)]
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -451,7 +507,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     d2h = world * 4 * hq.numel() * hq.element_size()
 
     # a job takes as long as its slowest rank
-    t_ms, e2e_ms, t_fwd, t_bwd = max_over_ranks([t_ms, e2e_ms, t_fwd, t_bwd], device=dev)
+    t_ms, e2e_ms, t_fwd, t_bwd, t_eager = max_over_ranks([t_ms, e2e_ms, t_fwd, t_bwd, t_eager], device=dev)
 
     peaks, peak_src = load_peaks()
     value = flops_job * args.steps / (t_ms / 1e3) / 1e12
@@ -521,6 +577,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": t_ms / args.steps,
+            "eager_ms_per_step": t_eager / eager_steps,
             "higher_is_better": True,
             "scaling": "weak" if args.weak else "strong",
             "vs_baseline": None,
@@ -534,7 +591,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                                        f"{world} rank(s), one whole problem each, no collective"),
                        "flops_per_step_per_rank": flops_step,
                        "flops_per_step_job": flops_job,
-                       "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush"},
+                       "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush",
+                       "timing": ("CUDA-graph replays of one captured step (public-API forward + autograd backward); "
+                                  "eager_ms_per_step: the same step launched eagerly" if graph is not None else
+                                  f"eager steps (graph capture unavailable: {graph_err or 'disabled by --eager'})")},
             "weak_scaling": weak,
             "per_gpu_tflops": value / world,
             "pct_of_bf16_peak_sustained": 100.0 * value / world / float(
@@ -562,6 +622,32 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def capture_step(fn, dev: torch.device):
+    """(graph, None) with ``fn`` captured as a CUDA graph after two warm-up calls on a side stream
+    and one checked replay, or (None, reason) when capture fails."""
+    from quantumdlblocks_b200.kernels import flash_born as fbm
+
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        rc, site = fbm.device_status()
+        if rc != 0:
+            raise RuntimeError(f"device status {rc} (site {site}) after the graph's first replay")
+        return graph, None
+    except Exception as exc:  # noqa: BLE001 -- report it and time eagerly
+        return None, f"{type(exc).__name__}: {str(exc)[:160]}"
 
 
 def run_other_workload(args, workload: str, rank: int, world: int, dev: torch.device, flush: torch.Tensor,
@@ -597,6 +683,7 @@ def run_other_workload(args, workload: str, rank: int, world: int, dev: torch.de
     for _ in range(2):
         step()
     torch.cuda.synchronize()
+    graph, graph_err = (None, "disabled by --eager") if args.eager else capture_step(step, dev)
     if world > 1:
         dist.barrier()
     steps = args.extra_steps
@@ -605,7 +692,10 @@ def run_other_workload(args, workload: str, rank: int, world: int, dev: torch.de
     for i in range(steps):
         flush.zero_()
         ev[i][0].record()
-        step()
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
         ev[i][1].record()
     torch.cuda.synchronize()
     t_ms = sum(a.elapsed_time(b) for a, b in ev)
@@ -640,10 +730,12 @@ def run_other_workload(args, workload: str, rank: int, world: int, dev: torch.de
                       "parallelism": f"(batch, head) units split over {world} ranks, rank 0 holds batch "
                                      f"[{shard.b0},{shard.b1}) x heads [{shard.h0},{shard.h1}); no collective",
                       "flops_per_step_job": 14.0 * D * pairs_full,
-                      "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush"},
+                      "l2": "flushed before every step (256 MiB write); per-step CUDA events exclude the flush",
+                      "timing": "CUDA-graph replays of one captured step" if graph is not None else
+                                f"eager steps ({graph_err})"},
            "fwd_ms": t_fwd, "bwd_ms": t_bwd, "bwd_tflops_per_gpu": bwd_tf, "bwd_frac": bwd_tf / peak,
            "peak_source": "bf16_tflops (burst), measured"}
-    del q, k, v, do, doc, scale, qd, kd, vd, out_d, z_d
+    del q, k, v, do, doc, scale, qd, kd, vd, out_d, z_d, graph
     torch.cuda.empty_cache()
     return res
 
@@ -986,6 +1078,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpt", action="store_true", help="skip the C5 GPT training-step measurement")
+    ap.add_argument("--eager", action="store_true", help="time the steps eagerly instead of as CUDA-graph replays")
     ap.add_argument("--extra-steps", type=int, default=5,
                     help="steps of C3 and C4 timed in the default C2 run (0 skips them)")
     ap.add_argument("--gpt-steps", type=int, default=10)

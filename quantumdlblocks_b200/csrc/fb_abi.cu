@@ -6,6 +6,8 @@
 // device memory: the backward's scratch comes from the caller's workspace.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "fb_common.cuh"
@@ -177,6 +179,26 @@ int run(const fb_attn_args* a, void* stream, bool purified, bool backward, bool 
 }  // namespace
 
 void set_last_launch_count(int n) { t_last_launches = n; }
+
+cudaError_t set_smem_limit_once(const void* kernel, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const std::pair<const void*, int> key(kernel, dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= smem) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(mu);
+  int& v = done[key];
+  v = std::max(v, smem);
+  return cudaSuccess;
+}
 
 void record_cuda_error(cudaError_t e) {
   const char* msg = cudaGetErrorString(e);

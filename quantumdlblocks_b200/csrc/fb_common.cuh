@@ -226,6 +226,10 @@ int tc_bwd64(const Problem& p, cudaStream_t s, int* launches);
 size_t tc_bwd64_workspace(const Problem& p);
 void record_cuda_error(cudaError_t e);
 void set_last_launch_count(int n);  // what fb_last_launch_count reports for this host thread
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) for `kernel` on the current device, made once
+// per (kernel, device, size) and remembered (a failure is not), so that repeated launches spend
+// no host time on it and a launch inside a stream capture makes no attribute call
+cudaError_t set_smem_limit_once(const void* kernel, int smem);
 // document-mask tile ranges (fb_docs.cu): bytes of workspace, and the two launches that fill it
 size_t doc_ranges_bytes(const Problem& p);
 int doc_ranges(const Problem& p, cudaStream_t s, void* ws, DocRanges* out);

@@ -534,7 +534,7 @@ int kd_bucket(int D) { return D <= 32 ? 32 : D <= 64 ? 64 : D <= 128 ? 128 : 256
 template <typename K>
 int launch(K kernel, dim3 grid, size_t smem, cudaStream_t s, const GenArgs& a) {
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = set_smem_limit_once(reinterpret_cast<const void*>(kernel), (int)smem);
     if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   }
   kernel<<<grid, kThreads, smem, s>>>(a);

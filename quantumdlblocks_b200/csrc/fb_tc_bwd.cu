@@ -1155,7 +1155,7 @@ int launch_kv(cudaStream_t s, const BwdParams& bp, const CUtensorMap& mk, const 
               const CUtensorMap& mdo) {
   auto kernel = tc_dkdv_kernel<D, Map, kHasDoc>;
   const uint32_t smem = KvCfg<D>::kSmem + 1024;  // + alignment slack
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_limit_once(reinterpret_cast<const void*>(kernel), (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   kernel<<<std::min(bp.n_items, bwd_num_sms()), kThreads, smem, s>>>(mk, mv, mq, mdo, bp);
   e = cudaGetLastError();
@@ -1168,7 +1168,7 @@ int launch_dq(cudaStream_t s, const BwdParams& bp, const CUtensorMap& mq, const 
               const CUtensorMap& mv) {
   auto kernel = tc_dq_kernel<D, Map, kHasDoc>;
   const uint32_t smem = DqCfg<D>::kSmem + 1024;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_limit_once(reinterpret_cast<const void*>(kernel), (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   kernel<<<std::min(bp.n_qitems, bwd_num_sms()), kThreads, smem, s>>>(mq, mdo, mk, mv, bp);
   e = cudaGetLastError();

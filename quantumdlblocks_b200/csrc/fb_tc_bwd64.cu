@@ -904,7 +904,7 @@ int launch_main(const Problem& pr, cudaStream_t s, const BwdParams& bp, const CU
                 const CUtensorMap& mdv) {
   auto kernel = tc_bwd_kernel<Map, kHasDoc>;
   const uint32_t smem = kSmemBytes + 1024;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_limit_once(reinterpret_cast<const void*>(kernel), (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   dim3 grid(std::min(bp.n_items, bwd_num_sms()));
   kernel<<<grid, kThreads, smem, s>>>(mk, mv, mq, mdo, mdq, mdk, mdv, bp);

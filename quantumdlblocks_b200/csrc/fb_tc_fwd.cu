@@ -685,7 +685,7 @@ int launch_fwd(const Problem& pr, cudaStream_t s, const FwdParams& fp, const CUt
                const CUtensorMap& mv) {
   auto kernel = tc_fwd_kernel<D, Map, kHasDoc, TO>;
   const uint32_t smem = FwdCfg<D>::kSmemBytes + 1024;  // + alignment slack
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_limit_once(reinterpret_cast<const void*>(kernel), (int)smem);
   if (e != cudaSuccess) { record_cuda_error(e); return FB_ERR_LAUNCH; }
   dim3 grid(std::min(fp.n_items, num_sms()));
   kernel<<<grid, FwdCfg<D>::kThreads, smem, s>>>(mq, mk, mv, fp);
