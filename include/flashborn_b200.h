@@ -114,7 +114,8 @@ typedef struct fb_attn_args {
   float* dtau;   /* accumulated, tau_numel elements (purified) */
 
   /* Backward: fb_bwd_workspace_size() bytes.  Forward: fb_fwd_workspace_size() bytes, which is
-   * non-zero only with doc_ids on the tensor-core path (document spans used to skip tiles). */
+   * non-zero only with doc_ids on the tensor-core path (document spans used to skip tiles, and the
+   * runs of equal ids that turn the document mask into one range per row). */
   void* workspace; size_t workspace_bytes;
 } fb_attn_args;
 
@@ -263,7 +264,8 @@ FB_API size_t fb_bwd_workspace_size(const fb_attn_args* args);
 
 /* Bytes of device workspace the forward needs for these arguments: 0 without doc_ids; with them,
  * room for the per-64-row-block document spans that let the tensor-core kernels skip tiles with
- * no same-document pair.  ABI version 2.  No counterpart in the reference (its forward visits
+ * no same-document pair, and for the per-position runs of equal ids (about batch * seq_len * 8
+ * bytes) with which rows whose ids never decrease mask by one range.  ABI version 2.  No counterpart in the reference (its forward visits
  * every causal tile and masks, flash_born.py:169-178). */
 FB_API size_t fb_fwd_workspace_size(const fb_attn_args* args);
 
